@@ -1,0 +1,62 @@
+// Kernel-level entry points for the GPU test-suite: each runs one kernel of the evaluator on
+// caller-owned device buffers, so every kernel can be checked on its own against a plain
+// fp32 reference before the whole forward pass is compared with the CPU oracle.
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/marina_b200.h"
+#include "gemm.h"
+
+namespace {
+thread_local char g_test_error[512];
+
+int fail(const char* msg) {
+  snprintf(g_test_error, sizeof(g_test_error), "%s", msg);
+  return MRN_ERR_ARGUMENT;
+}
+
+int num_sms() {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+}  // namespace
+
+extern "C" {
+
+const char* mrn_test_last_error(void) { return g_test_error; }
+
+int mrn_test_gemm(int fp8, int epilogue, const void* a, const void* b, const float* bias, void* out, int ldo, int m,
+                  int n, int k, float scale, float inv_q, int* status, void* stream) {
+  static bool prepared = false;
+  if (!prepared) {
+    if (mrn::gemm_prepare_device() != cudaSuccess) return fail("gemm_prepare_device failed");
+    prepared = true;
+  }
+  mrn::GemmArgs args;
+  args.a = a;
+  args.b = b;
+  args.m = m;
+  args.n = n;
+  args.k = k;
+  args.fp8 = fp8 != 0;
+  args.epi = static_cast<mrn::Epilogue>(epilogue);
+  args.out = out;
+  args.ldo = ldo;
+  args.bias = bias;
+  args.scale = scale;
+  args.inv_q = inv_q;
+  args.status = status;
+  mrn::GemmPlan plan;
+  char err[256];
+  if (!mrn::gemm_plan(&plan, args, num_sms(), err)) return fail(err);
+  const cudaError_t e = mrn::gemm_launch(plan, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    snprintf(g_test_error, sizeof(g_test_error), "gemm launch: %s", cudaGetErrorString(e));
+    return MRN_ERR_CUDA;
+  }
+  return MRN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,130 @@
+// Instantiations and host dispatch of the tcgen05 GEMM.
+#include <stdio.h>
+
+#include "gemm.cuh"
+#include "gemm.h"
+#include "tmap.h"
+
+namespace mrn {
+
+namespace {
+
+template <int BN, bool FP8, class Epi>
+cudaError_t launch_one(const GemmPlan& p, const Epi& epi, cudaStream_t stream) {
+  gemm_tc_kernel<BN, FP8, Epi><<<p.grid, kGemmThreads, GemmShape<BN>::kSmemBytes, stream>>>(
+      p.map_a, p.map_b, epi, p.args.m, p.args.n, p.args.k, p.args.status);
+  return cudaGetLastError();
+}
+
+template <int BN, bool FP8>
+cudaError_t launch_bn(const GemmPlan& p, cudaStream_t stream) {
+  const GemmArgs& a = p.args;
+  switch (a.epi) {
+    case Epilogue::kBias:
+      return launch_one<BN, FP8>(p, EpiBiasBf16{static_cast<__nv_bfloat16*>(a.out), a.ldo, a.bias, a.scale}, stream);
+    case Epilogue::kResidual:
+      return launch_one<BN, FP8>(p, EpiResidual{static_cast<float*>(a.out), a.ldo, a.bias, a.scale}, stream);
+    case Epilogue::kGeluBf16:
+      if constexpr (!FP8) return launch_one<BN, FP8>(p, EpiGelu<false>{a.out, a.ldo, a.bias, a.scale, a.inv_q}, stream);
+      break;
+    case Epilogue::kGeluE4m3:
+      if constexpr (FP8) return launch_one<BN, FP8>(p, EpiGelu<true>{a.out, a.ldo, a.bias, a.scale, a.inv_q}, stream);
+      break;
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <bool FP8>
+cudaError_t launch_fp8(const GemmPlan& p, cudaStream_t stream) {
+  switch (p.bn) {
+    case 256: return launch_bn<256, FP8>(p, stream);
+    case 192: return launch_bn<192, FP8>(p, stream);
+    case 128: return launch_bn<128, FP8>(p, stream);
+    case 64: return launch_bn<64, FP8>(p, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <int BN, bool FP8, class Epi>
+cudaError_t prepare_one() {
+  return cudaFuncSetAttribute(gemm_tc_kernel<BN, FP8, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              GemmShape<BN>::kSmemBytes);
+}
+
+template <int BN>
+cudaError_t prepare_bn() {
+  cudaError_t e;
+  if ((e = prepare_one<BN, false, EpiBiasBf16>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, false, EpiResidual>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, false, EpiGelu<false>>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, true, EpiBiasBf16>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, true, EpiResidual>()) != cudaSuccess) return e;
+  return prepare_one<BN, true, EpiGelu<true>>();
+}
+
+}  // namespace
+
+int gemm_pick_bn(int n) {
+  for (int bn : {256, 192, 128, 64})
+    if (n % bn == 0) return bn;
+  return 0;
+}
+
+bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
+  plan->args = args;
+  plan->bn = gemm_pick_bn(args.n);
+  const int eb = args.fp8 ? 1 : 2;
+  if (args.m <= 0 || args.n <= 0 || args.k <= 0) {
+    snprintf(err, 256, "gemm: empty shape %dx%dx%d", args.m, args.n, args.k);
+    return false;
+  }
+  if (plan->bn == 0) {
+    snprintf(err, 256, "gemm: N=%d is not a multiple of 64", args.n);
+    return false;
+  }
+  if ((args.k * eb) % 16 != 0) {
+    snprintf(err, 256, "gemm: K=%d rows are not a multiple of 16 bytes", args.k);
+    return false;
+  }
+  if (args.epi == Epilogue::kGeluE4m3 && !args.fp8) {
+    snprintf(err, 256, "gemm: e4m3 GELU output is only planned for FP8 operands");
+    return false;
+  }
+  if (args.epi == Epilogue::kGeluBf16 && args.fp8) {
+    snprintf(err, 256, "gemm: bf16 GELU output is only planned for bf16 operands");
+    return false;
+  }
+  if (args.ldo < args.n || (reinterpret_cast<uintptr_t>(args.out) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(args.bias) & 15) != 0) {
+    snprintf(err, 256, "gemm: output/bias misaligned or ldo %d < N %d", args.ldo, args.n);
+    return false;
+  }
+  if (!make_kmajor_map(&plan->map_a, args.a, eb, args.m, args.k, kTileM) ||
+      !make_kmajor_map(&plan->map_b, args.b, eb, args.n, args.k, plan->bn)) {
+    snprintf(err, 256, "gemm: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", args.m, args.n, args.k);
+    return false;
+  }
+  const int tiles = ((args.m + kTileM - 1) / kTileM) * (args.n / plan->bn);
+  plan->grid = tiles < num_sms ? tiles : num_sms;
+  switch (plan->bn) {
+    case 256: plan->smem = GemmShape<256>::kSmemBytes; break;
+    case 192: plan->smem = GemmShape<192>::kSmemBytes; break;
+    case 128: plan->smem = GemmShape<128>::kSmemBytes; break;
+    default: plan->smem = GemmShape<64>::kSmemBytes; break;
+  }
+  return true;
+}
+
+cudaError_t gemm_prepare_device() {
+  cudaError_t e;
+  if ((e = prepare_bn<256>()) != cudaSuccess) return e;
+  if ((e = prepare_bn<192>()) != cudaSuccess) return e;
+  if ((e = prepare_bn<128>()) != cudaSuccess) return e;
+  return prepare_bn<64>();
+}
+
+cudaError_t gemm_launch(const GemmPlan& plan, cudaStream_t stream) {
+  return plan.args.fp8 ? launch_fp8<true>(plan, stream) : launch_fp8<false>(plan, stream);
+}
+
+}  // namespace mrn

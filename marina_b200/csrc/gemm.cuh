@@ -1,0 +1,313 @@
+// Persistent warp-specialised tcgen05 GEMM for the encoder's linear layers:
+//
+//     D[M, N] = A[M, K] · B[N, K]^T        (A = activations, B = a Linear's weight, both K-major)
+//
+// followed by a fused epilogue (bias, GELU, residual add, re-quantisation). One CTA per SM
+// walks the output tiles (128 rows x BN columns) in n-fastest order, so the CTAs working on
+// the same 128-row block of A at the same time share it through L2.
+//
+// Roles (192 threads):
+//   warp 0, one lane : TMA producer. A 128x128-byte tile and a BNx128-byte tile per stage,
+//                      128-byte swizzled, into a STAGES-deep ring of shared-memory buffers.
+//   warp 1, one lane : MMA issuer. 4 tcgen05.mma (K = 32 bytes each) per stage into a TMEM
+//                      accumulator; two accumulators of BN columns alternate between tiles
+//                      so the epilogue of one tile overlaps the MMAs of the next.
+//   warps 2..5       : epilogue. Warp w reads TMEM lanes 32*(w%4).. (one output row per
+//                      thread) 32 columns at a time and applies the epilogue functor.
+//
+// Operands are bf16 (kind::f16, K-step 64 per stage) or e4m3 (kind::f8f6f4, K-step 128 per
+// stage); either way a stage row is 128 bytes. K tails and M tails are zero-filled by TMA.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include "ptx.cuh"
+
+namespace mrn {
+
+constexpr int kGemmThreads = 192;
+constexpr int kTileM = 128;
+constexpr int kStageRowBytes = 128;  // one swizzle row: 64 bf16 or 128 e4m3 values of K
+constexpr uint32_t kTmemCols = 512;  // two accumulators of up to 256 f32 columns
+
+template <int BN>
+struct GemmShape {
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
+  static constexpr int kABytes = kTileM * kStageRowBytes;
+  static constexpr int kBBytes = BN * kStageRowBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  // As many stages as fit next to the barriers in the 227 KB a CTA may use.
+  static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes = 1024 /*alignment slack*/ + kStages * kStageBytes + kBarrierBytes;
+};
+
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752f)); }
+
+// ---- epilogues -------------------------------------------------------------------------
+// Each receives one row's 32 consecutive accumulator columns starting at `col`.
+
+// out[row, col..] = bf16(acc * scale + bias)
+struct EpiBiasBf16 {
+  __nv_bfloat16* out;
+  int ldo;
+  const float* bias;
+  float scale;
+  __device__ __forceinline__ void apply(int row, int col, const float (&v)[32]) const {
+    __nv_bfloat16* o = out + static_cast<size_t>(row) * ldo + col;
+#pragma unroll
+    for (int c = 0; c < 32; c += 8) {
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + col + c));
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + col + c + 4));
+      __nv_bfloat162 p[4];
+      p[0] = __floats2bfloat162_rn(v[c + 0] * scale + b0.x, v[c + 1] * scale + b0.y);
+      p[1] = __floats2bfloat162_rn(v[c + 2] * scale + b0.z, v[c + 3] * scale + b0.w);
+      p[2] = __floats2bfloat162_rn(v[c + 4] * scale + b1.x, v[c + 5] * scale + b1.y);
+      p[3] = __floats2bfloat162_rn(v[c + 6] * scale + b1.z, v[c + 7] * scale + b1.w);
+      *reinterpret_cast<uint4*>(o + c) = *reinterpret_cast<const uint4*>(p);
+    }
+  }
+};
+
+// out[row, col..] = GELU(acc * scale + bias), stored as bf16, or as e4m3 codes of
+// value * inv_q (saturating) when E4M3.
+template <bool E4M3>
+struct EpiGelu {
+  void* out;
+  int ldo;
+  const float* bias;
+  float scale;
+  float inv_q;
+  __device__ __forceinline__ void apply(int row, int col, const float (&v)[32]) const {
+    float g[32];
+#pragma unroll
+    for (int c = 0; c < 32; c += 4) {
+      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c));
+      g[c + 0] = gelu_erf(v[c + 0] * scale + b.x);
+      g[c + 1] = gelu_erf(v[c + 1] * scale + b.y);
+      g[c + 2] = gelu_erf(v[c + 2] * scale + b.z);
+      g[c + 3] = gelu_erf(v[c + 3] * scale + b.w);
+    }
+    if constexpr (E4M3) {
+      uint8_t* o = static_cast<uint8_t*>(out) + static_cast<size_t>(row) * ldo + col;
+#pragma unroll
+      for (int c = 0; c < 32; c += 16) {
+        __nv_fp8x2_storage_t q[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          q[j] = __nv_cvt_float2_to_fp8x2(make_float2(g[c + 2 * j] * inv_q, g[c + 2 * j + 1] * inv_q), __NV_SATFINITE,
+                                          __NV_E4M3);
+        *reinterpret_cast<uint4*>(o + c) = *reinterpret_cast<const uint4*>(q);
+      }
+    } else {
+      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(row) * ldo + col;
+#pragma unroll
+      for (int c = 0; c < 32; c += 8) {
+        __nv_bfloat162 p[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) p[j] = __floats2bfloat162_rn(g[c + 2 * j], g[c + 2 * j + 1]);
+        *reinterpret_cast<uint4*>(o + c) = *reinterpret_cast<const uint4*>(p);
+      }
+    }
+  }
+};
+
+// x[row, col..] += acc * scale + bias   (the f32 residual stream)
+struct EpiResidual {
+  float* x;
+  int ldx;
+  const float* bias;
+  float scale;
+  __device__ __forceinline__ void apply(int row, int col, const float (&v)[32]) const {
+    float* xr = x + static_cast<size_t>(row) * ldx + col;
+#pragma unroll
+    for (int c = 0; c < 32; c += 4) {
+      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c));
+      float4 r = *reinterpret_cast<const float4*>(xr + c);
+      r.x += v[c + 0] * scale + b.x;
+      r.y += v[c + 1] * scale + b.y;
+      r.z += v[c + 2] * scale + b.z;
+      r.w += v[c + 3] * scale + b.w;
+      *reinterpret_cast<float4*>(xr + c) = r;
+    }
+  }
+};
+
+// ---- the kernel ------------------------------------------------------------------------
+template <int BN, bool FP8, class Epi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Epi epi,
+                   int M, int N, int K, int* status) {
+  using S = GemmShape<BN>;
+  constexpr int kStages = S::kStages;
+  constexpr int kElemsPerStage = FP8 ? 128 : 64;
+  constexpr uint32_t kIdesc = FP8 ? idesc_e4m3(kTileM, BN) : idesc_bf16(kTileM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the 128-byte swizzle atoms.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm_a = smem;
+  uint8_t* sm_b = smem + kStages * S::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * S::kStageBytes);
+  uint64_t* full = bars;                   // [kStages] TMA -> MMA
+  uint64_t* empty = bars + kStages;        // [kStages] MMA -> TMA
+  uint64_t* tmem_full = bars + 2 * kStages;   // [2] MMA -> epilogue
+  uint64_t* tmem_empty = tmem_full + 2;       // [2] epilogue -> MMA
+  uint64_t* drain = tmem_empty + 2;           // [1] MMA completion on abort
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_tiles = N / BN;
+  const int m_tiles = (M + kTileM - 1) / kTileM;
+  const int total = m_tiles * n_tiles;
+  const int k_blocks = (K + kElemsPerStage - 1) / kElemsPerStage;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_barrier_init();
+    tma_prefetch_map(&map_a);
+    tma_prefetch_map(&map_b);
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, parity_mask = 0;  // per stage: a load was issued, and in which phase
+      for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * kTileM;
+        const int n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort)) {
+            raise_error(status, abort, kErrTimeoutProducer);
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+          tma_load_2d(sm_a + stage * S::kABytes, &map_a, &full[stage], kb * kElemsPerStage, m0);
+          tma_load_2d(sm_b + stage * S::kBBytes, &map_b, &full[stage], kb * kElemsPerStage, n0);
+          issued_mask |= 1u << stage;
+          parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (*abort) {
+        // Let the copies still in flight land before the CTA's shared memory goes away.
+        for (int s = 0; s < kStages; ++s)
+          if (issued_mask & (1u << s)) mbar_wait_bounded(&full[s], (parity_mask >> s) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool issued = false;
+      for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort)) {
+          raise_error(status, abort, kErrTimeoutMma);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort)) {
+            raise_error(status, abort, kErrTimeoutMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sm_a + stage * S::kABytes);
+          const uint32_t b_addr = smem_u32(sm_b + stage * S::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kStageRowBytes / 32; ++k) {
+            const uint64_t ad = desc_sw128(a_addr + 32u * k);
+            const uint64_t bd = desc_sw128(b_addr + 32u * k);
+            if constexpr (FP8)
+              mma_e4m3(d, ad, bd, kIdesc, (kb | k) != 0);
+            else
+              mma_bf16(d, ad, bd, kIdesc, (kb | k) != 0);
+          }
+          issued = true;
+          tc_commit(&empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tmem_full[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (*abort && issued) {
+        // Let the MMAs already issued finish before their buffers and TMEM go away.
+        tc_commit(drain);
+        if (!mbar_wait_bounded(drain, 0) && status) atomicCAS(status, 0, kErrTimeoutDrain);
+      }
+    }
+  } else {
+    // ---- epilogue: warps 2..5 cover TMEM lane quarters 2, 3, 0, 1
+    const int quarter = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+      const int m0 = (tile / n_tiles) * kTileM;
+      const int n0 = (tile % n_tiles) * BN;
+      if (!mbar_wait(&tmem_full[acc], acc_phase, abort)) {
+        if (lane == 0) raise_error(status, abort, kErrTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(taddr + c, v);
+        if (row < M) epi.apply(row, n0 + c, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace mrn

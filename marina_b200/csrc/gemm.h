@@ -1,0 +1,56 @@
+// Host interface of the tcgen05 GEMM (gemm.cuh): a plan (tensor maps + launch shape) is
+// built once per (buffer, batch bucket) and launched many times, including inside CUDA
+// graphs.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace mrn {
+
+enum class Epilogue : int {
+  kBias = 0,       // out bf16 = acc*scale + bias                  (QKV projection)
+  kGeluBf16 = 1,   // out bf16 = GELU(acc*scale + bias)            (FFN1, bf16 activations)
+  kGeluE4m3 = 2,   // out e4m3 = GELU(acc*scale + bias) * inv_q    (FFN1, FP8 activations)
+  kResidual = 3,   // x f32 += acc*scale + bias                    (out-proj, FFN2)
+};
+
+struct GemmArgs {
+  const void* a = nullptr;  // activations [M, K], bf16 or e4m3, row-major
+  const void* b = nullptr;  // weight [N, K], same type, row-major (PyTorch Linear layout)
+  int m = 0, n = 0, k = 0;
+  bool fp8 = false;          // operands are e4m3 (kind::f8f6f4) instead of bf16 (kind::f16)
+  Epilogue epi = Epilogue::kBias;
+  void* out = nullptr;       // bf16 / e4m3 output, or the f32 residual stream
+  int ldo = 0;               // row stride of `out` in elements
+  const float* bias = nullptr;  // [N]
+  float scale = 1.f;         // dequantisation of the accumulator (weight scale x activation scale)
+  float inv_q = 1.f;         // 1 / output quantisation scale (kGeluE4m3)
+  int* status = nullptr;     // device error word (first error wins)
+};
+
+struct GemmPlan {
+  CUtensorMap map_a;
+  CUtensorMap map_b;
+  GemmArgs args;
+  int bn = 0;
+  int grid = 0;
+  int smem = 0;
+};
+
+// Widest supported N tile (256, 192, 128, 64) dividing n; 0 if none.
+int gemm_pick_bn(int n);
+
+// Validate shapes and alignment and build the tensor maps. `err` (>= 256 bytes) receives a
+// message on failure.
+bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err);
+
+// Opt every kernel instantiation into its dynamic shared memory size (once per device).
+cudaError_t gemm_prepare_device();
+
+cudaError_t gemm_launch(const GemmPlan& plan, cudaStream_t stream);
+
+// Algorithmic FLOPs of one launch (2·M·N·K).
+inline double gemm_flops(const GemmArgs& a) { return 2.0 * a.m * static_cast<double>(a.n) * a.k; }
+
+}  // namespace mrn

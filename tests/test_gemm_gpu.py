@@ -1,0 +1,103 @@
+"""The tcgen05 GEMM (every epilogue, bf16 and e4m3 operands) against a plain PyTorch fp32
+reference of the same op, at the encoder's shapes (`nano` 192/576/768, `small`
+512/1536/2048) with ragged row counts (B·65 rows is never a multiple of the 128-row tile)."""
+
+import ctypes
+
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from marina_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+EPI_BIAS, EPI_GELU_BF16, EPI_GELU_E4M3, EPI_RESIDUAL = 0, 1, 2, 3
+
+# (M, N, K): QKV, out-proj, FFN1, FFN2 of both nets; M = positions x 65.
+SHAPES = [
+    (65 * 3, 576, 192), (65 * 3, 192, 192), (65 * 3, 768, 192), (65 * 3, 192, 768),
+    (65 * 7, 1536, 512), (65 * 7, 512, 512), (65 * 7, 2048, 512), (65 * 7, 512, 2048),
+    (1, 256, 64), (128, 128, 128), (65 * 64, 1536, 512),
+]
+
+
+def _run(fp8, epi, a, b, bias, out, ldo, m, n, k, scale=1.0, inv_q=1.0):
+    lib = _lib.load()
+    status = torch.zeros(1, dtype=torch.int32, device=a.device)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.mrn_test_gemm(int(fp8), epi, a.data_ptr(), b.data_ptr(), bias.data_ptr(), out.data_ptr(), ldo, m, n, k,
+                           scale, inv_q, ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(stream))
+    assert rc == 0, lib.mrn_test_last_error().decode()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, f"device status {int(status.item())}"
+
+
+def _operands(m, n, k, fp8, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    a = torch.randn(m, k, device="cuda", generator=g)
+    b = torch.randn(n, k, device="cuda", generator=g) * 0.05
+    bias = torch.randn(n, device="cuda", generator=g) * 0.1
+    if fp8:
+        a8 = a.to(torch.float8_e4m3fn)
+        b8 = (b * 8).to(torch.float8_e4m3fn)
+        return a8.view(torch.uint8), b8.view(torch.uint8), a8.float(), b8.float(), bias
+    ab, bb = a.to(torch.bfloat16), b.to(torch.bfloat16)
+    return ab, bb, ab.float(), bb.float(), bias
+
+
+@pytest.mark.parametrize("fp8", [False, True], ids=["bf16", "e4m3"])
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_bias_epilogue(cuda, fp8, m, n, k):
+    a, b, af, bf, bias = _operands(m, n, k, fp8, seed=m + n + k)
+    scale = 0.125 if fp8 else 1.0
+    out = torch.full((m, n), float("nan"), device=cuda, dtype=torch.bfloat16)
+    _run(fp8, EPI_BIAS, a, b, bias, out, n, m, n, k, scale=scale)
+    ref = (af @ bf.T) * scale + bias
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
+
+
+@pytest.mark.parametrize("m,n,k", [s for s in SHAPES if s[1] in (768, 2048, 256)])
+def test_gelu_bf16_epilogue(cuda, m, n, k):
+    a, b, af, bf, bias = _operands(m, n, k, False, seed=7)
+    out = torch.zeros((m, n), device=cuda, dtype=torch.bfloat16)
+    _run(False, EPI_GELU_BF16, a, b, bias, out, n, m, n, k)
+    ref = torch.nn.functional.gelu(af @ bf.T + bias)
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
+
+
+@pytest.mark.parametrize("m,n,k", [s for s in SHAPES if s[1] in (768, 2048, 256)])
+def test_gelu_e4m3_epilogue(cuda, m, n, k):
+    a, b, af, bf, bias = _operands(m, n, k, True, seed=11)
+    scale, q = 0.125, 0.05  # output value = code * q
+    out = torch.zeros((m, n), device=cuda, dtype=torch.uint8)
+    _run(True, EPI_GELU_E4M3, a, b, bias, out, n, m, n, k, scale=scale, inv_q=1.0 / q)
+    ref = torch.nn.functional.gelu((af @ bf.T) * scale + bias)
+    got = out.view(torch.float8_e4m3fn).float() * q
+    # one e4m3 rounding step (3 mantissa bits) plus saturation at 448 * q
+    tol = ref.abs() * 0.0625 + q * 2 ** -6
+    ref_sat = ref.clamp(-448 * q, 448 * q)
+    assert bool(((got - ref_sat).abs() <= tol + 1e-6).all())
+
+
+@pytest.mark.parametrize("fp8", [False, True], ids=["bf16", "e4m3"])
+@pytest.mark.parametrize("m,n,k", [s for s in SHAPES if s[1] in (192, 512, 128)])
+def test_residual_epilogue(cuda, fp8, m, n, k):
+    a, b, af, bf, bias = _operands(m, n, k, fp8, seed=3)
+    scale = 0.125 if fp8 else 1.0
+    x0 = torch.randn(m, n, device=cuda)
+    x = x0.clone()
+    _run(fp8, EPI_RESIDUAL, a, b, bias, x, n, m, n, k, scale=scale)
+    ref = x0 + (af @ bf.T) * scale + bias
+    err = (x - ref).abs().max().item()
+    assert err <= 1e-4 * ref.abs().max().item() + 1e-5, err
+
+
+def test_rows_beyond_m_untouched(cuda):
+    m, n, k = 65 * 3, 576, 192
+    a, b, af, bf, bias = _operands(m, n, k, False, seed=5)
+    out = torch.full((m + 128, n), 7.0, device=cuda, dtype=torch.bfloat16)
+    _run(False, EPI_BIAS, a, b, bias, out, n, m, n, k)
+    assert bool((out[m:] == 7.0).all())
