@@ -1,0 +1,326 @@
+"""Throughput of the B200 evaluator on Marina's hot path: the batched transformer forward the
+PUCT search calls on each leaf minibatch (src/net/mod.rs:290-296, src/search/mod.rs:686).
+
+One step = one forward pass of a batch of synthetic leaf positions (uniform-random legal
+playouts of 0-80 plies, encoded as the reference encodes them) through the `small` network
+(d_model 512, 12 layers, 8 heads, d_ff 2048, random init N(0, 0.02) seed 0, per-tensor e4m3
+weights) on every GPU. Each GPU holds a full weight replica and evaluates its own batch (weak
+scaling, no collective on the data path; NCCL only carries the barrier and the max over ranks).
+
+    python bench.py [--gpus N --steps K --warmup W --batch B --net small|nano --precision fp8|fp8w|bf16]
+    python bench.py --impl reference ...   # the reference's CPU backend (its C restatement) on host cores
+
+Prints one JSON line (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "small-net evals/sec per B200 and 8xB200 at batch 256-8192; PUCT nodes/sec"
+UNIT = "evals/s"
+L2_BYTES = 126 * 2 ** 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--net", choices=["small", "nano"], default="small")
+    ap.add_argument("--batch", type=int, default=4096, help="positions per GPU per step")
+    ap.add_argument("--precision", choices=["fp8", "fp8w", "bf16"], default="fp8")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_net(name: str):
+    from marina_b200 import model, weights
+
+    arch = model.Architecture.from_json((ROOT / "marina_b200" / "cards" / f"{name}.json").read_text())
+    w = weights.random_init(arch, seed=0)
+    return arch, w
+
+
+def workload_config(args, n_gpus: int) -> dict:
+    return {
+        "workload": f"{args.net} net forward (configs[1] network: d512 L12 8x64 ff2048, e4m3 per-tensor weights)"
+        if args.net == "small" else "nano net forward (d192 L6 6x32 ff768)",
+        "net": args.net,
+        "batch_per_gpu": args.batch,
+        "global_batch": args.batch * n_gpus,
+        "tokens_per_position": 65,
+        "precision": args.precision,
+        "parallelism": f"replicas{n_gpus} (no collective)",
+        "inputs": "uniform-random legal playouts, 0-80 plies, per-rank seed",
+        "l2": "activations (>1 GB per step) exceed the 126 MB L2; a 256 MiB buffer is also rewritten between timed steps",
+    }
+
+
+def flops_per_eval(arch) -> float:
+    d, ff, t, L = arch.d_model, arch.d_ff, arch.tokens, arch.n_layers
+    return 2.0 * t * L * (4 * d * d + 2 * d * ff)
+
+
+# ---- CPU baseline: the oracle (C restatement of src/net/cpu.rs) on the host cores ---------
+def cpu_baseline(args, arch, w, seconds: float) -> dict:
+    import oracle
+    from marina_b200 import chess, weights
+
+    threads = os.cpu_count() or 1
+    wq = weights.fp8_weights(w) if args.precision != "bf16" else w
+    net = oracle.OracleNetwork(arch, wq, threads=threads)
+    # every thread gets at least one 512-row slice (src/net/cpu.rs:352 slices rows the same way)
+    chunk = min(max(8 * threads, 16), 2048)
+    boards, legal, _, _ = chess.random_positions(4242, chunk)
+    net.evaluate(boards[:2], legal[:2])  # warm
+    done, t0 = 0, time.perf_counter()
+    while True:
+        net.evaluate(boards, legal)
+        done += chunk
+        el = time.perf_counter() - t0
+        if el >= seconds or el > 0 and done / el * seconds < chunk * 0.5:
+            break
+    el = time.perf_counter() - t0
+    return {"value": done / el, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{done} positions of the {args.net} config ({chunk}-position batches) in {el:.1f} s"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    arch, w = load_net(args.net)
+    import oracle
+    from marina_b200 import chess, weights
+
+    threads = os.cpu_count() or 1
+    wq = weights.fp8_weights(w) if args.precision != "bf16" else w
+    net = oracle.OracleNetwork(arch, wq, threads=threads)
+    sample = min(max(8 * threads, 16), 2048)
+    boards, legal, _, _ = chess.random_positions(4242, sample)
+    for _ in range(args.warmup):
+        net.evaluate(boards, legal)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        net.evaluate(boards, legal)
+    el = time.perf_counter() - t0
+    value = sample * args.steps / el
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args, args.gpus) | {"batch_per_step": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{sample} positions per step of the {args.net} config"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's CPU backend (src/net/cpu.rs) is Rust and no Rust toolchain exists here; "
+                "this arm times its C restatement (oracle/) on all host threads",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---- clocks during the timed region ---------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device, self.proc, self.lines = device, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from marina_b200 import _lib, chess
+    from marina_b200.network import B200Network
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    arch, w = load_net(args.net)
+    B = args.batch
+    net = B200Network(arch, w, device=local, max_batch=B, precision=args.precision)
+    boards, legal, counts, _ = chess.random_positions(1 + 1000 * rank, B, 0, 80)
+    stream = torch.cuda.current_stream(dev)
+
+    # device-resident inputs / outputs
+    d_boards = torch.from_numpy(boards).to(dev)
+    d_legal = torch.from_numpy(legal).to(dev)
+    d_priors = torch.empty((B, 224), device=dev)
+    d_wdl = torch.empty((B, 3), device=dev)
+    flush = torch.empty(256 * 2 ** 20 // 4, device=dev)
+
+    def step_device():
+        net.evaluate_device(B, d_boards.data_ptr(), d_legal.data_ptr(), d_priors.data_ptr(), d_wdl.data_ptr(),
+                            stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step_device()
+    torch.cuda.synchronize()
+    if net.status_word() != 0:
+        raise SystemExit("device fault during warm-up")
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            starts[i].record(stream)
+            step_device()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms_steps = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms = max_over_ranks(float(np.sum(ms_steps)) / args.steps)
+    value = world * B / (ms / 1e3)
+    if net.status_word() != 0:
+        raise SystemExit("device fault during the timed steps")
+
+    # end to end through the public API with pinned host buffers
+    h_boards = torch.from_numpy(boards).pin_memory()
+    h_legal = torch.from_numpy(legal).pin_memory()
+    h_priors = torch.empty((B, 224)).pin_memory()
+    h_wdl = torch.empty((B, 3)).pin_memory()
+    nb, nl, npr, nw = (t.numpy() for t in (h_boards, h_legal, h_priors, h_wdl))
+    for _ in range(max(1, args.warmup)):
+        net.evaluate_packed(nb, nl, npr, nw)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        net.evaluate_packed(nb, nl, npr, nw)
+    e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
+    e2e_value = world * B / e2e_s
+
+    # roofline of the dominant kernel (the GEMM): one eager pass with events around each launch
+    prof = net.profile(B, d_boards.data_ptr(), d_legal.data_ptr(), d_priors.data_ptr(), d_wdl.data_ptr(),
+                       stream.cuda_stream)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    bf16_peak = peaks.get("bf16_tflops")
+    if bf16_peak:
+        peak, peak_src = (2 * bf16_peak, "2x measured bf16 burst (MEASURED_PEAKS.json has no fp8 figure)") \
+            if args.precision == "fp8" else (bf16_peak, "measured bf16 burst (MEASURED_PEAKS.json)")
+    else:
+        peak, peak_src = (2 * 1590.0, "2x fallback bf16") if args.precision == "fp8" else (1590.0, "fallback bf16")
+    g = prof["gemm"]
+    achieved = g["flops"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else 0.0
+    total_prof_ms = sum(v["ms"] for v in prof.values())
+
+    launches = net.launches_per_forward(B) * args.steps
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": {"fp8": "e4m3", "fp8w": "bf16", "bf16": "bf16"}[args.precision],
+            "data": "synthetic (seeded random-playout positions; random-init weights)",
+            "config": workload_config(args, world),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None, "kernel": "gemm_tc_kernel (all GEMM launches of one pass)",
+                         "peak_source": peak_src, "flops_per_eval": flops_per_eval(arch)},
+            "kernel_ms": {k: round(v["ms"], 4) for k, v in prof.items()},
+            "kernel_share": {k: round(v["ms"] / total_prof_ms, 4) for k, v in prof.items()} if total_prof_ms else {},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(B * (66 + 224 * 4)),
+                    "d2h_bytes_per_step": int(B * (224 * 4 + 3 * 4 + 4)), "ms_per_step": e2e_s * 1e3,
+                    "path": "mrn_evaluate (C ABI) on pinned host buffers: H2D, graph replay, D2H, sync"},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+            "describe": net.describe(),
+        }
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = cpu_baseline(args, arch, w, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    net.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

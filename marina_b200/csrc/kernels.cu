@@ -1,0 +1,520 @@
+// The evaluator's non-GEMM kernels: token embedding (fused with layer 0's norm1), warp-per-row
+// LayerNorm, per-(position, head) attention on the tensor cores, the legal-move policy head
+// and the value head's output layer. See kernels.cuh for the data layout.
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include "kernels.cuh"
+
+namespace mrn {
+
+namespace {
+
+constexpr int kPlanes = 73;
+constexpr int kActions = 64 * kPlanes;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---- one row of d values held by a warp -------------------------------------------------
+// Lane l holds VPL = d/32 values as VPL/VEC chunks of VEC consecutive elements; chunk c sits
+// at element (c*32 + l)*VEC, so every chunk step is one coalesced warp-wide access.
+template <int VPL, int VEC>
+struct WarpRow {
+  static constexpr int kChunks = VPL / VEC;
+  float v[VPL];
+
+  __device__ __forceinline__ static int col(int c, int lane) { return (c * 32 + lane) * VEC; }
+
+  __device__ __forceinline__ void load(const float* __restrict__ src, int lane) {
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      if constexpr (VEC == 4) {
+        const float4 q = *reinterpret_cast<const float4*>(src + col(c, lane));
+        v[c * 4 + 0] = q.x, v[c * 4 + 1] = q.y, v[c * 4 + 2] = q.z, v[c * 4 + 3] = q.w;
+      } else {
+        const float2 q = *reinterpret_cast<const float2*>(src + col(c, lane));
+        v[c * 2 + 0] = q.x, v[c * 2 + 1] = q.y;
+      }
+    }
+  }
+
+  __device__ __forceinline__ void store(float* __restrict__ dst, int lane) const {
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      if constexpr (VEC == 4)
+        *reinterpret_cast<float4*>(dst + col(c, lane)) = make_float4(v[c * 4], v[c * 4 + 1], v[c * 4 + 2], v[c * 4 + 3]);
+      else
+        *reinterpret_cast<float2*>(dst + col(c, lane)) = make_float2(v[c * 2], v[c * 2 + 1]);
+    }
+  }
+
+  // In place: LayerNorm over the d values (biased variance, two passes, as PyTorch).
+  __device__ __forceinline__ void layernorm(const float* __restrict__ g, const float* __restrict__ b, float eps,
+                                            int d, int lane) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) s += v[i];
+    const float mean = warp_sum(s) / static_cast<float>(d);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) q += (v[i] - mean) * (v[i] - mean);
+    const float inv = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(d) + eps);
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const int k = col(c, lane) + e;
+        v[c * VEC + e] = (v[c * VEC + e] - mean) * inv * __ldg(g + k) + __ldg(b + k);
+      }
+    }
+  }
+
+  __device__ __forceinline__ void store_act(void* dst, ActType type, float inv_q, int lane) const {
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      const float* x = v + c * VEC;
+      if (type == ActType::kBf16) {
+        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(dst) + col(c, lane);
+        if constexpr (VEC == 4) {
+          __nv_bfloat162 p[2] = {__floats2bfloat162_rn(x[0], x[1]), __floats2bfloat162_rn(x[2], x[3])};
+          *reinterpret_cast<uint2*>(o) = *reinterpret_cast<const uint2*>(p);
+        } else {
+          *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(x[0], x[1]);
+        }
+      } else {
+        uint8_t* o = static_cast<uint8_t*>(dst) + col(c, lane);
+        if constexpr (VEC == 4) {
+          __nv_fp8x2_storage_t p[2] = {
+              __nv_cvt_float2_to_fp8x2(make_float2(x[0] * inv_q, x[1] * inv_q), __NV_SATFINITE, __NV_E4M3),
+              __nv_cvt_float2_to_fp8x2(make_float2(x[2] * inv_q, x[3] * inv_q), __NV_SATFINITE, __NV_E4M3)};
+          *reinterpret_cast<uint32_t*>(o) = *reinterpret_cast<const uint32_t*>(p);
+        } else {
+          *reinterpret_cast<__nv_fp8x2_storage_t*>(o) =
+              __nv_cvt_float2_to_fp8x2(make_float2(x[0] * inv_q, x[1] * inv_q), __NV_SATFINITE, __NV_E4M3);
+        }
+      }
+    }
+  }
+};
+
+// ---- embedding + layer 0 norm1 (src/net/cpu.rs:59-84, src/net/cuda/kernels.cu:69-100) ----
+template <int VPL, int VEC>
+__global__ void __launch_bounds__(256) embed_ln_kernel(EmbedParams e, NormParams n, int rows, int d) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  using Row = WarpRow<VPL, VEC>;
+  Row r;
+  const int pos = row / e.t, i = row - pos * e.t;
+  const uint8_t* b = e.boards + static_cast<size_t>(pos) * 66;
+  if (i == 0) {
+    const uint8_t castling = b[64];
+    const int ep = b[65] < 8 ? b[65] : 8;
+#pragma unroll
+    for (int c = 0; c < Row::kChunks; ++c)
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) {
+        const int o = Row::col(c, lane) + k;
+        const float* w = e.castling_w + static_cast<size_t>(o) * 4;
+        float s = 0.f;
+#pragma unroll
+        for (int bit = 0; bit < 4; ++bit) s += __ldg(w + bit) * static_cast<float>((castling >> bit) & 1);
+        r.v[c * VEC + k] = (__ldg(e.state_embed + o) + (__ldg(e.castling_b + o) + s)) +
+                           __ldg(e.ep_embed + static_cast<size_t>(ep) * d + o);
+      }
+  } else if (i >= e.square_start && i < e.square_start + 64) {
+    const int s = i - e.square_start;
+    const int piece = b[s] < 13 ? b[s] : 0;
+#pragma unroll
+    for (int c = 0; c < Row::kChunks; ++c)
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) {
+        const int o = Row::col(c, lane) + k;
+        r.v[c * VEC + k] =
+            __ldg(e.piece_embed + static_cast<size_t>(piece) * d + o) + __ldg(e.square_embed + static_cast<size_t>(s) * d + o);
+      }
+  } else {
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) r.v[k] = 0.f;
+  }
+  r.store(e.x + static_cast<size_t>(row) * d, lane);
+  r.layernorm(n.gamma, n.beta, n.eps, d, lane);
+  const size_t off = static_cast<size_t>(row) * d * (n.out_type == ActType::kBf16 ? 2 : 1);
+  r.store_act(static_cast<uint8_t*>(n.out) + off, n.out_type, n.inv_q, lane);
+}
+
+// ---- LayerNorm, one warp per row (src/net/cpu.rs:323-343) --------------------------------
+template <int VPL, int VEC>
+__global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, NormParams n, int rows, int d) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  WarpRow<VPL, VEC> r;
+  r.load(x + static_cast<size_t>(row) * d, lane);
+  r.layernorm(n.gamma, n.beta, n.eps, d, lane);
+  const size_t off = static_cast<size_t>(row) * d * (n.out_type == ActType::kBf16 ? 2 : 1);
+  r.store_act(static_cast<uint8_t*>(n.out) + off, n.out_type, n.inv_q, lane);
+}
+
+// ---- attention ---------------------------------------------------------------------------
+// One CTA per (position, head); Q, K and V of the head (t <= 80 rows, zero-padded to 80) live
+// in shared memory. Warp w owns query rows 16w..16w+15: S = Q K^T for its strip stays in
+// registers (mma.sync m16n8k16, f32 accumulation), the softmax runs on the accumulators with
+// quad shuffles, and the probabilities feed P V straight from registers.
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+
+__device__ __forceinline__ uint32_t lds32(const __nv_bfloat16* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+constexpr int kAttnRows = 80;
+constexpr int kAttnWarps = kAttnRows / 16;
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(AttentionParams p) {
+  constexpr int LD = HD + 8;  // bf16 elements per staged row (16-byte multiple, conflict-free)
+  constexpr int CH = HD / 8;  // 16-byte chunks per row
+  __shared__ __align__(16) __nv_bfloat16 sq[kAttnRows * LD];
+  __shared__ __align__(16) __nv_bfloat16 sk[kAttnRows * LD];
+  __shared__ __align__(16) __nv_bfloat16 sv[kAttnRows * LD];
+
+  const int t = p.t, d = p.d;
+  const int pos = blockIdx.x / p.heads;
+  const int head = blockIdx.x - pos * p.heads;
+  const __nv_bfloat16* base =
+      static_cast<const __nv_bfloat16*>(p.qkv) + static_cast<size_t>(pos) * t * 3 * d + head * HD;
+  for (int i = threadIdx.x; i < kAttnRows * CH; i += blockDim.x) {
+    const int row = i / CH, ch = i - row * CH;
+    uint4 q = make_uint4(0, 0, 0, 0), k = q, v = q;
+    if (row < t) {
+      const __nv_bfloat16* r = base + static_cast<size_t>(row) * 3 * d + ch * 8;
+      q = *reinterpret_cast<const uint4*>(r);
+      k = *reinterpret_cast<const uint4*>(r + d);
+      v = *reinterpret_cast<const uint4*>(r + 2 * d);
+    }
+    *reinterpret_cast<uint4*>(sq + row * LD + ch * 8) = q;
+    *reinterpret_cast<uint4*>(sk + row * LD + ch * 8) = k;
+    *reinterpret_cast<uint4*>(sv + row * LD + ch * 8) = v;
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const int r0 = warp * 16;
+  if (r0 >= t) return;
+
+  // S = Q K^T for rows r0..r0+15 against all 80 (padded) keys.
+  float s[10][4];
+#pragma unroll
+  for (int nt = 0; nt < 10; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < HD; kk += 16) {
+    uint32_t a[4];
+    a[0] = lds32(sq + (r0 + g) * LD + kk + 2 * tq);
+    a[1] = lds32(sq + (r0 + g + 8) * LD + kk + 2 * tq);
+    a[2] = lds32(sq + (r0 + g) * LD + kk + 8 + 2 * tq);
+    a[3] = lds32(sq + (r0 + g + 8) * LD + kk + 8 + 2 * tq);
+#pragma unroll
+    for (int nt = 0; nt < 10; ++nt) {
+      const __nv_bfloat16* kr = sk + (nt * 8 + g) * LD + kk + 2 * tq;
+      mma_16816(s[nt], a, lds32(kr), lds32(kr + 8));
+    }
+  }
+
+  // Softmax of rows g (values 0,1) and g+8 (values 2,3) of the strip; keys >= t are masked.
+  const float scale_log2 = rsqrtf(static_cast<float>(HD)) * 1.4426950408889634f;
+  float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+  for (int nt = 0; nt < 10; ++nt)
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      if (nt * 8 + 2 * tq + j < t) {
+        m0 = fmaxf(m0, s[nt][j]);
+        m1 = fmaxf(m1, s[nt][2 + j]);
+      }
+  m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
+  m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
+  m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+  m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
+  float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+  for (int nt = 0; nt < 10; ++nt)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const bool valid = nt * 8 + 2 * tq + j < t;
+      s[nt][j] = valid ? exp2f((s[nt][j] - m0) * scale_log2) : 0.f;
+      s[nt][2 + j] = valid ? exp2f((s[nt][2 + j] - m1) * scale_log2) : 0.f;
+      l0 += s[nt][j];
+      l1 += s[nt][2 + j];
+    }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+  // O = P V: P comes from the S accumulators (two n-tiles make one k16 A fragment).
+  float o[HD / 8][4];
+#pragma unroll
+  for (int nt = 0; nt < HD / 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < 5; ++kk) {
+    uint32_t a[4];
+    a[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+    a[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+    a[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+    a[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+    const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+    for (int nt = 0; nt < HD / 8; nt += 2) {
+      uint32_t b[4];
+      ldmatrix_x4_trans(b, sv + key * LD + nt * 8 + ((lane >> 4) & 1) * 8);
+      mma_16816(o[nt], a, b[0], b[1]);
+      mma_16816(o[nt + 1], a, b[2], b[3]);
+    }
+  }
+
+  const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int row = r0 + g + half * 8;
+    if (row >= t) continue;
+    const float inv = half ? inv1 : inv0;
+    const size_t at = (static_cast<size_t>(pos) * t + row) * d + head * HD + 2 * tq;
+#pragma unroll
+    for (int nt = 0; nt < HD / 8; ++nt) {
+      const float v0 = o[nt][2 * half] * inv, v1 = o[nt][2 * half + 1] * inv;
+      if (p.out_type == ActType::kBf16) {
+        *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.out) + at + nt * 8) =
+            __floats2bfloat162_rn(v0, v1);
+      } else {
+        *reinterpret_cast<__nv_fp8x2_storage_t*>(static_cast<uint8_t*>(p.out) + at + nt * 8) =
+            __nv_cvt_float2_to_fp8x2(make_float2(v0 * p.inv_q, v1 * p.inv_q), __NV_SATFINITE, __NV_E4M3);
+      }
+    }
+  }
+}
+
+// ---- heads -----------------------------------------------------------------------------
+// One CTA (8 warps) per position. Each warp takes legal slots in turn: the slot's square token
+// gets the final norm and the policy norm in registers (src/net/cpu.rs:137,140-152) and its
+// logit is bias[plane] + <token, W[plane]> (src/net/cuda/kernels.cu:407-444 gathers the same
+// logits). Warp 0 also normalises the state token for the value head's first layer. The
+// softmax over the legal slots is block-wide (src/net/cpu.rs:177-178).
+constexpr int kHeadsWarps = 8;
+
+template <int VPL, int VEC>
+__global__ void __launch_bounds__(kHeadsWarps * 32) heads_kernel(HeadsParams p, int d) {
+  extern __shared__ float logits[];  // [slots] when p.softmax
+  __shared__ float red[kHeadsWarps];
+  using Row = WarpRow<VPL, VEC>;
+  const int pos = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t row0 = static_cast<size_t>(pos) * p.t;
+
+  if (warp == 0) {
+    Row r;
+    r.load(p.x + row0 * d, lane);
+    r.layernorm(p.final_g, p.final_b, p.eps, d, lane);
+    r.layernorm(p.value_g, p.value_b, p.eps, d, lane);
+    r.store_act(static_cast<__nv_bfloat16*>(p.value_in) + static_cast<size_t>(pos) * d, ActType::kBf16, 1.f, lane);
+  }
+
+  for (int slot = warp; slot < p.slots; slot += kHeadsWarps) {
+    const int action = p.legal ? p.legal[static_cast<size_t>(pos) * p.slots + slot] : slot;
+    float logit = -INFINITY;
+    if (action >= kActions) {
+      if (lane == 0 && p.status) atomicCAS(p.status, 0, kErrBadAction);
+    } else if (action >= 0) {
+      const int square = action / kPlanes, plane = action - square * kPlanes;
+      Row r;
+      r.load(p.x + (row0 + p.square_start + square) * d, lane);
+      r.layernorm(p.final_g, p.final_b, p.eps, d, lane);
+      r.layernorm(p.policy_g, p.policy_b, p.eps, d, lane);
+      const float* w = p.policy_w + static_cast<size_t>(plane) * d;
+      float acc = 0.f;
+#pragma unroll
+      for (int c = 0; c < Row::kChunks; ++c)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc += r.v[c * VEC + e] * __ldg(w + Row::col(c, lane) + e);
+      logit = warp_sum(acc) + __ldg(p.policy_bias + plane);
+    }
+    if (lane == 0) {
+      if (p.softmax)
+        logits[slot] = logit;
+      else
+        p.priors[static_cast<size_t>(pos) * p.slots + slot] = logit;
+    }
+  }
+  if (!p.softmax) return;
+  __syncthreads();
+
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < p.slots; i += blockDim.x) m = fmaxf(m, logits[i]);
+  m = warp_max(m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  m = red[0];
+#pragma unroll
+  for (int w = 1; w < kHeadsWarps; ++w) m = fmaxf(m, red[w]);
+  __syncthreads();
+  float sum = 0.f;
+  for (int i = threadIdx.x; i < p.slots; i += blockDim.x) {
+    const float e = logits[i] == -INFINITY ? 0.f : expf(logits[i] - m);
+    logits[i] = e;
+    sum += e;
+  }
+  sum = warp_sum(sum);
+  if (lane == 0) red[warp] = sum;
+  __syncthreads();
+  sum = 0.f;
+#pragma unroll
+  for (int w = 0; w < kHeadsWarps; ++w) sum += red[w];
+  const float inv = 1.f / fmaxf(sum, 1.17549435e-38f);
+  for (int i = threadIdx.x; i < p.slots; i += blockDim.x)
+    p.priors[static_cast<size_t>(pos) * p.slots + i] = logits[i] * inv;
+}
+
+// Value head output layer and softmax, one warp per position (src/net/cpu.rs:161-162,179-180).
+template <int VPL, int VEC>
+__global__ void __launch_bounds__(256) value_out_kernel(ValueOutParams p, int positions, int d) {
+  const int lane = threadIdx.x & 31;
+  const int pos = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (pos >= positions) return;
+  using Row = WarpRow<VPL, VEC>;
+  const __nv_bfloat16* h = static_cast<const __nv_bfloat16*>(p.hidden) + static_cast<size_t>(pos) * d;
+  float acc[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < Row::kChunks; ++c)
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const int k = Row::col(c, lane) + e;
+      const float hv = __bfloat162float(h[k]);
+#pragma unroll
+      for (int o = 0; o < 3; ++o) acc[o] += hv * __ldg(p.w2 + o * d + k);
+    }
+  float z[3];
+#pragma unroll
+  for (int o = 0; o < 3; ++o) z[o] = warp_sum(acc[o]) + __ldg(p.b2 + o);
+  if (lane == 0) {
+    float* out = p.wdl + static_cast<size_t>(pos) * 3;
+    if (p.softmax) {
+      const float m = fmaxf(z[0], fmaxf(z[1], z[2]));
+      const float e0 = expf(z[0] - m), e1 = expf(z[1] - m), e2 = expf(z[2] - m);
+      const float inv = 1.f / (e0 + e1 + e2);
+      out[0] = e0 * inv, out[1] = e1 * inv, out[2] = e2 * inv;
+    } else {
+      out[0] = z[0], out[1] = z[1], out[2] = z[2];
+    }
+  }
+}
+
+// Dispatch on d (a multiple of 64 up to 1024): values per lane and vector width.
+template <template <int, int> class Launch, class... Args>
+cudaError_t dispatch_d(int d, Args&&... args) {
+  switch (d) {
+    case 64: return Launch<2, 2>::run(d, args...);
+    case 128: return Launch<4, 4>::run(d, args...);
+    case 192: return Launch<6, 2>::run(d, args...);
+    case 256: return Launch<8, 4>::run(d, args...);
+    case 320: return Launch<10, 2>::run(d, args...);
+    case 384: return Launch<12, 4>::run(d, args...);
+    case 448: return Launch<14, 2>::run(d, args...);
+    case 512: return Launch<16, 4>::run(d, args...);
+    case 640: return Launch<20, 4>::run(d, args...);
+    case 768: return Launch<24, 4>::run(d, args...);
+    case 1024: return Launch<32, 4>::run(d, args...);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <int VPL, int VEC>
+struct EmbedLaunch {
+  static cudaError_t run(int d, const EmbedParams& e, const NormParams& n, int positions, cudaStream_t s) {
+    const int rows = positions * e.t;
+    embed_ln_kernel<VPL, VEC><<<(rows + 7) / 8, 256, 0, s>>>(e, n, rows, d);
+    return cudaGetLastError();
+  }
+};
+
+template <int VPL, int VEC>
+struct NormLaunch {
+  static cudaError_t run(int d, const float* x, const NormParams& n, int rows, cudaStream_t s) {
+    layernorm_kernel<VPL, VEC><<<(rows + 7) / 8, 256, 0, s>>>(x, n, rows, d);
+    return cudaGetLastError();
+  }
+};
+
+template <int VPL, int VEC>
+struct HeadsLaunch {
+  static cudaError_t run(int d, const HeadsParams& p, int positions, cudaStream_t s) {
+    const size_t smem = p.softmax ? sizeof(float) * p.slots : 0;
+    heads_kernel<VPL, VEC><<<positions, kHeadsWarps * 32, smem, s>>>(p, d);
+    return cudaGetLastError();
+  }
+};
+
+template <int VPL, int VEC>
+struct ValueOutLaunch {
+  static cudaError_t run(int d, const ValueOutParams& p, int positions, cudaStream_t s) {
+    value_out_kernel<VPL, VEC><<<(positions + 7) / 8, 256, 0, s>>>(p, positions, d);
+    return cudaGetLastError();
+  }
+};
+
+}  // namespace
+
+cudaError_t launch_embed_ln(const EmbedParams& e, const NormParams& n, int positions, int d, cudaStream_t s) {
+  return dispatch_d<EmbedLaunch>(d, e, n, positions, s);
+}
+
+cudaError_t launch_layernorm(const float* x, const NormParams& n, int rows, int d, cudaStream_t s) {
+  return dispatch_d<NormLaunch>(d, x, n, rows, s);
+}
+
+cudaError_t launch_attention(const AttentionParams& p, int positions, int head_dim, cudaStream_t s) {
+  if (p.t > kAttnRows) return cudaErrorInvalidValue;
+  const int blocks = positions * p.heads;
+  if (head_dim == 64)
+    attention_kernel<64><<<blocks, kAttnWarps * 32, 0, s>>>(p);
+  else if (head_dim == 32)
+    attention_kernel<32><<<blocks, kAttnWarps * 32, 0, s>>>(p);
+  else
+    return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_heads(const HeadsParams& p, int positions, int d, cudaStream_t s) {
+  return dispatch_d<HeadsLaunch>(d, p, positions, s);
+}
+
+cudaError_t launch_value_out(const ValueOutParams& p, int positions, int d, cudaStream_t s) {
+  return dispatch_d<ValueOutLaunch>(d, p, positions, s);
+}
+
+}  // namespace mrn

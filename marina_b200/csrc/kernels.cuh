@@ -1,0 +1,82 @@
+// Launchers of the evaluator's non-GEMM kernels (kernels.cu). Layout: a batch of B positions
+// is R = B*t token rows (t = 65: the state token, then 64 squares), row r = pos*t + i.
+// The residual stream x is f32 [R, d]; GEMM operands are bf16 or e4m3 rows.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mrn {
+
+// Activation storage of a GEMM operand produced by a kernel.
+enum class ActType : int { kBf16 = 0, kE4m3 = 1 };
+
+struct EmbedParams {
+  const uint8_t* boards;     // [B, 66]
+  const float* piece_embed;  // [13, d]
+  const float* square_embed; // [64, d]
+  const float* state_embed;  // [d]
+  const float* castling_w;   // [d, 4]
+  const float* castling_b;   // [d]
+  const float* ep_embed;     // [9, d]
+  float* x;                  // [R, d]
+  int t, square_start;
+};
+
+struct NormParams {
+  const float* gamma;
+  const float* beta;
+  float eps;
+  void* out;       // bf16 or e4m3 [R, d]
+  ActType out_type;
+  float inv_q;     // 1 / e4m3 scale
+};
+
+// x = tokens(boards); out = LN(x) (layer 0's norm1) in one pass.
+cudaError_t launch_embed_ln(const EmbedParams& e, const NormParams& n, int positions, int d, cudaStream_t s);
+// out = LN(x) for rows [0, rows).
+cudaError_t launch_layernorm(const float* x, const NormParams& n, int rows, int d, cudaStream_t s);
+
+struct AttentionParams {
+  const void* qkv;   // bf16 [R, 3d]: Q | K | V, head h at columns h*hd
+  void* out;         // bf16 or e4m3 [R, d]
+  ActType out_type;
+  float inv_q;
+  int t, d, heads;
+};
+cudaError_t launch_attention(const AttentionParams& p, int positions, int head_dim, cudaStream_t s);
+
+struct HeadsParams {
+  const float* x;             // [R, d] residual stream after the last layer
+  const float* final_g;       // final_norm
+  const float* final_b;
+  const float* policy_g;      // policy_head.norm
+  const float* policy_b;
+  const float* policy_w;      // [73, d] f32
+  const float* policy_bias;   // [73]
+  const float* value_g;       // value_head.norm
+  const float* value_b;
+  const int32_t* legal;       // [B, slots] action indices, -1 padded; NULL = every action in order
+  int slots;                  // 224, or 4672 for raw logits
+  int softmax;                // 1: priors (softmax over the legal slots), 0: raw logits
+  float* priors;              // [B, slots]
+  void* value_in;             // bf16 [B, d]: LN_value(LN_final(x[pos, 0])) for the value GEMM
+  int* status;                // device error word: action index out of range
+  float eps;
+  int t, square_start;
+};
+cudaError_t launch_heads(const HeadsParams& p, int positions, int d, cudaStream_t s);
+
+struct ValueOutParams {
+  const void* hidden;   // bf16 [B, d] GELU(value_ff1)
+  const float* w2;      // [3, d]
+  const float* b2;      // [3]
+  float* wdl;           // [B, 3]
+  int softmax;          // 1: probabilities, 0: logits
+};
+cudaError_t launch_value_out(const ValueOutParams& p, int positions, int d, cudaStream_t s);
+
+// Device error codes raised by these kernels (the GEMM uses 1..4).
+constexpr int kErrBadAction = 16;
+
+}  // namespace mrn

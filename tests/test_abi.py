@@ -1,0 +1,77 @@
+"""The C-ABI libraries load and export every symbol their headers declare, and the
+evaluator's argument checks run (and fail cleanly) without a GPU."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from marina_b200 import _lib, chess, model, weights
+from marina_b200.network import B200Network, NetworkError
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared(header: str, macro: str) -> list[str]:
+    text = (ROOT / "include" / header).read_text()
+    return re.findall(macro + r"\s+[\w\s\*]*?\b(m\w+)\(", text)
+
+
+def test_evaluator_exports_every_declared_symbol():
+    names = _declared("marina_b200.h", "MRN_API")
+    assert "mrn_create" in names and "mrn_evaluate" in names and len(names) >= 12
+    lib = _lib.load()
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(_lib.EXPORTS) >= set(names)
+
+
+def test_chess_library_exports_every_declared_symbol():
+    names = _declared("marina_chess.h", "MRC_API")
+    lib = chess.load()
+    assert len(names) >= 13
+    for name in names:
+        assert hasattr(lib, name), name
+
+
+def _create(arch, w, precision="bf16"):
+    return B200Network(arch, w, device=0, max_batch=8, precision=precision)
+
+
+def test_unsupported_architectures_are_refused_before_touching_a_device():
+    w_arch = model.Architecture(192, 1, 4, 768)  # head dim 48
+    with pytest.raises(NetworkError) as e:
+        _create(w_arch, weights.random_init(w_arch))
+    assert e.value.code == 5 and "head dimension 48" in str(e.value)
+    arch = model.nano()
+    arch.fp8_amax = None
+    with pytest.raises(NetworkError) as e:
+        _create(arch, weights.random_init(arch), precision="fp8")
+    assert e.value.code == 1 and "calibration" in str(e.value)
+
+
+def test_non_finite_weights_are_refused():
+    arch = model.Architecture(64, 1, 2, 128)
+    w = weights.random_init(arch)
+    w.tensors["encoder.layers.0.linear1.weight"][3, 5] = np.nan
+    with pytest.raises(NetworkError) as e:
+        _create(arch, w)
+    assert e.value.code == 1 and "linear1.weight" in str(e.value)
+
+
+def test_create_without_a_cuda_device_reports_an_error(monkeypatch):
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    arch = model.Architecture(64, 1, 2, 128)
+    with pytest.raises(NetworkError) as e:
+        _create(arch, weights.random_init(arch))
+    assert e.value.code in (2, 5)
+
+
+def test_precision_names():
+    arch = model.Architecture(64, 1, 2, 128)
+    with pytest.raises(ValueError):
+        B200Network(arch, weights.random_init(arch), precision="fp32")
