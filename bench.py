@@ -219,7 +219,10 @@ def run_ours(args):
     B = args.batch
     net = B200Network(arch, w, device=local, max_batch=B, precision=args.precision)
     boards, legal, counts, _ = chess.random_positions(1 + 1000 * rank, B, 0, 80)
-    stream = torch.cuda.current_stream(dev)
+    # A created stream: the events and the forward pass must be ordered on the same stream
+    # (the library runs a NULL-stream request on its own non-blocking stream).
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
 
     # device-resident inputs / outputs
     d_boards = torch.from_numpy(boards).to(dev)

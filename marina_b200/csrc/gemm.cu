@@ -12,7 +12,7 @@ namespace {
 template <int BN, bool FP8, class Epi>
 cudaError_t launch_one(const GemmPlan& p, const Epi& epi, cudaStream_t stream) {
   gemm_tc_kernel<BN, FP8, Epi><<<p.grid, kGemmThreads, GemmShape<BN>::kSmemBytes, stream>>>(
-      p.map_a, p.map_b, epi, p.args.m, p.args.n, p.args.k, p.args.status);
+      p.map_a, p.map_b, p.map_out, epi, p.args.m, p.args.n, p.args.k, p.args.status);
   return cudaGetLastError();
 }
 
@@ -21,14 +21,14 @@ cudaError_t launch_bn(const GemmPlan& p, cudaStream_t stream) {
   const GemmArgs& a = p.args;
   switch (a.epi) {
     case Epilogue::kBias:
-      return launch_one<BN, FP8>(p, EpiBiasBf16{static_cast<__nv_bfloat16*>(a.out), a.ldo, a.bias, a.scale}, stream);
+      return launch_one<BN, FP8>(p, EpiBiasBf16{a.bias, a.scale}, stream);
     case Epilogue::kResidual:
-      return launch_one<BN, FP8>(p, EpiResidual{static_cast<float*>(a.out), a.ldo, a.bias, a.scale}, stream);
+      return launch_one<BN, FP8>(p, EpiResidual{a.bias, a.scale}, stream);
     case Epilogue::kGeluBf16:
-      if constexpr (!FP8) return launch_one<BN, FP8>(p, EpiGelu<false>{a.out, a.ldo, a.bias, a.scale, a.inv_q}, stream);
+      if constexpr (!FP8) return launch_one<BN, FP8>(p, EpiGelu<false>{a.bias, a.scale, a.inv_q}, stream);
       break;
     case Epilogue::kGeluE4m3:
-      if constexpr (FP8) return launch_one<BN, FP8>(p, EpiGelu<true>{a.out, a.ldo, a.bias, a.scale, a.inv_q}, stream);
+      if constexpr (FP8) return launch_one<BN, FP8>(p, EpiGelu<true>{a.bias, a.scale, a.inv_q}, stream);
       break;
   }
   return cudaErrorInvalidValue;
@@ -102,6 +102,23 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
   if (!make_kmajor_map(&plan->map_a, args.a, eb, args.m, args.k, kTileM) ||
       !make_kmajor_map(&plan->map_b, args.b, eb, args.n, args.k, plan->bn)) {
     snprintf(err, 256, "gemm: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", args.m, args.n, args.k);
+    return false;
+  }
+  bool out_ok = false;
+  switch (args.epi) {
+    case Epilogue::kBias:
+    case Epilogue::kGeluBf16:
+      out_ok = make_store_map(&plan->map_out, args.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, args.m, args.n, args.ldo);
+      break;
+    case Epilogue::kGeluE4m3:
+      out_ok = make_store_map(&plan->map_out, args.out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, args.m, args.n, args.ldo);
+      break;
+    case Epilogue::kResidual:
+      out_ok = make_store_map(&plan->map_out, args.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, args.m, args.n, args.ldo);
+      break;
+  }
+  if (!out_ok) {
+    snprintf(err, 256, "gemm: output tensor map failed (M=%d N=%d ldo=%d)", args.m, args.n, args.ldo);
     return false;
   }
   const int tiles = ((args.m + kTileM - 1) / kTileM) * (args.n / plan->bn);

@@ -13,10 +13,14 @@
 //                      accumulator; two accumulators of BN columns alternate between tiles
 //                      so the epilogue of one tile overlaps the MMAs of the next.
 //   warps 2..5       : epilogue. Warp w reads TMEM lanes 32*(w%4).. (one output row per
-//                      thread) 32 columns at a time and applies the epilogue functor.
+//                      thread) 32 columns at a time, applies the epilogue functor, writes the
+//                      32x32 block into a swizzled shared-memory staging buffer and one lane
+//                      issues a TMA tile store (or, for the residual stream, a TMA reduce-add),
+//                      so global writes are whole swizzle rows issued by the copy engine.
 //
 // Operands are bf16 (kind::f16, K-step 64 per stage) or e4m3 (kind::f8f6f4, K-step 128 per
-// stage); either way a stage row is 128 bytes. K tails and M tails are zero-filled by TMA.
+// stage); either way a stage row is 128 bytes. K tails and M tails are zero-filled by TMA
+// on load and clipped by TMA on store.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -30,6 +34,11 @@ constexpr int kGemmThreads = 192;
 constexpr int kTileM = 128;
 constexpr int kStageRowBytes = 128;  // one swizzle row: 64 bf16 or 128 e4m3 values of K
 constexpr uint32_t kTmemCols = 512;  // two accumulators of up to 256 f32 columns
+constexpr int kEpiWarps = 4;
+constexpr int kEpiChunk = 32;                       // columns per epilogue step
+constexpr int kEpiBufBytes = 32 * kEpiChunk * 4;    // one 32x32 staging block at up to 4 B
+constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;  // double-buffered per warp
+constexpr int kMaxSmem = 232448;                    // 227 KB per CTA
 
 template <int BN>
 struct GemmShape {
@@ -37,25 +46,36 @@ struct GemmShape {
   static constexpr int kABytes = kTileM * kStageRowBytes;
   static constexpr int kBBytes = BN * kStageRowBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  // As many stages as fit next to the barriers in the 227 KB a CTA may use.
-  static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = 1024 /*alignment slack*/ + kStages * kStageBytes + kBarrierBytes;
+  static constexpr int kFit = (kMaxSmem - 1024 - kBarrierBytes - kEpiBytes) / kStageBytes;
+  static constexpr int kStages = kFit > 8 ? 8 : kFit;
+  static_assert(kStages >= 2, "not enough shared memory for a 2-stage pipeline");
+  static constexpr int kSmemBytes = 1024 /*alignment slack*/ + kStages * kStageBytes + kEpiBytes + kBarrierBytes;
 };
 
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752f)); }
 
-// ---- epilogues -------------------------------------------------------------------------
-// Each receives one row's 32 consecutive accumulator columns starting at `col`.
+// Byte offset of 16-byte chunk `j` of row `r` in a staging block whose rows are RB bytes and
+// which the TMA map reads with the matching swizzle (RB 128 -> 128B, 64 -> 64B, 32 -> 32B):
+// the swizzle XORs address bits [4, 4+log2(RB/16)) with bits [7, ...).
+template <int RB>
+__device__ __forceinline__ int staged_offset(int r, int j) {
+  if constexpr (RB == 128) return r * 128 + ((j ^ (r & 7)) << 4);
+  if constexpr (RB == 64) return r * 64 + ((j ^ ((r >> 1) & 3)) << 4);
+  return r * 32 + ((j ^ ((r >> 2) & 1)) << 4);
+}
 
-// out[row, col..] = bf16(acc * scale + bias)
+// ---- epilogues -------------------------------------------------------------------------
+// `pack` turns one row's 32 accumulator columns (starting at output column `col`) into the
+// row's kOutBytes*32 output bytes as 16-byte chunks.
+
+// out = bf16(acc * scale + bias)
 struct EpiBiasBf16 {
-  __nv_bfloat16* out;
-  int ldo;
+  static constexpr int kOutBytes = 2;
+  static constexpr bool kReduce = false;
   const float* bias;
   float scale;
-  __device__ __forceinline__ void apply(int row, int col, const float (&v)[32]) const {
-    __nv_bfloat16* o = out + static_cast<size_t>(row) * ldo + col;
+  __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[4]) const {
 #pragma unroll
     for (int c = 0; c < 32; c += 8) {
       const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + col + c));
@@ -65,21 +85,20 @@ struct EpiBiasBf16 {
       p[1] = __floats2bfloat162_rn(v[c + 2] * scale + b0.z, v[c + 3] * scale + b0.w);
       p[2] = __floats2bfloat162_rn(v[c + 4] * scale + b1.x, v[c + 5] * scale + b1.y);
       p[3] = __floats2bfloat162_rn(v[c + 6] * scale + b1.z, v[c + 7] * scale + b1.w);
-      *reinterpret_cast<uint4*>(o + c) = *reinterpret_cast<const uint4*>(p);
+      o[c / 8] = *reinterpret_cast<const uint4*>(p);
     }
   }
 };
 
-// out[row, col..] = GELU(acc * scale + bias), stored as bf16, or as e4m3 codes of
-// value * inv_q (saturating) when E4M3.
+// out = GELU(acc * scale + bias) as bf16, or as e4m3 codes of value * inv_q (saturating).
 template <bool E4M3>
 struct EpiGelu {
-  void* out;
-  int ldo;
+  static constexpr int kOutBytes = E4M3 ? 1 : 2;
+  static constexpr bool kReduce = false;
   const float* bias;
   float scale;
   float inv_q;
-  __device__ __forceinline__ void apply(int row, int col, const float (&v)[32]) const {
+  __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[kOutBytes * 2]) const {
     float g[32];
 #pragma unroll
     for (int c = 0; c < 32; c += 4) {
@@ -90,7 +109,6 @@ struct EpiGelu {
       g[c + 3] = gelu_erf(v[c + 3] * scale + b.w);
     }
     if constexpr (E4M3) {
-      uint8_t* o = static_cast<uint8_t*>(out) + static_cast<size_t>(row) * ldo + col;
 #pragma unroll
       for (int c = 0; c < 32; c += 16) {
         __nv_fp8x2_storage_t q[8];
@@ -98,38 +116,33 @@ struct EpiGelu {
         for (int j = 0; j < 8; ++j)
           q[j] = __nv_cvt_float2_to_fp8x2(make_float2(g[c + 2 * j] * inv_q, g[c + 2 * j + 1] * inv_q), __NV_SATFINITE,
                                           __NV_E4M3);
-        *reinterpret_cast<uint4*>(o + c) = *reinterpret_cast<const uint4*>(q);
+        o[c / 16] = *reinterpret_cast<const uint4*>(q);
       }
     } else {
-      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(row) * ldo + col;
 #pragma unroll
       for (int c = 0; c < 32; c += 8) {
         __nv_bfloat162 p[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) p[j] = __floats2bfloat162_rn(g[c + 2 * j], g[c + 2 * j + 1]);
-        *reinterpret_cast<uint4*>(o + c) = *reinterpret_cast<const uint4*>(p);
+        o[c / 8] = *reinterpret_cast<const uint4*>(p);
       }
     }
   }
 };
 
-// x[row, col..] += acc * scale + bias   (the f32 residual stream)
+// x += acc * scale + bias (the f32 residual stream), as a TMA reduce-add of the f32 values.
 struct EpiResidual {
-  float* x;
-  int ldx;
+  static constexpr int kOutBytes = 4;
+  static constexpr bool kReduce = true;
   const float* bias;
   float scale;
-  __device__ __forceinline__ void apply(int row, int col, const float (&v)[32]) const {
-    float* xr = x + static_cast<size_t>(row) * ldx + col;
+  __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[8]) const {
 #pragma unroll
     for (int c = 0; c < 32; c += 4) {
       const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c));
-      float4 r = *reinterpret_cast<const float4*>(xr + c);
-      r.x += v[c + 0] * scale + b.x;
-      r.y += v[c + 1] * scale + b.y;
-      r.z += v[c + 2] * scale + b.z;
-      r.w += v[c + 3] * scale + b.w;
-      *reinterpret_cast<float4*>(xr + c) = r;
+      float4 r = make_float4(v[c + 0] * scale + b.x, v[c + 1] * scale + b.y, v[c + 2] * scale + b.z,
+                             v[c + 3] * scale + b.w);
+      o[c / 4] = *reinterpret_cast<const uint4*>(&r);
     }
   }
 };
@@ -137,21 +150,23 @@ struct EpiResidual {
 // ---- the kernel ------------------------------------------------------------------------
 template <int BN, bool FP8, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Epi epi,
-                   int M, int N, int K, int* status) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   const __grid_constant__ CUtensorMap map_out, Epi epi, int M, int N, int K, int* status) {
   using S = GemmShape<BN>;
   constexpr int kStages = S::kStages;
   constexpr int kElemsPerStage = FP8 ? 128 : 64;
   constexpr uint32_t kIdesc = FP8 ? idesc_e4m3(kTileM, BN) : idesc_bf16(kTileM, BN);
+  constexpr int kRowBytes = kEpiChunk * Epi::kOutBytes;  // staged bytes per output row
 
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sm_a = smem;
   uint8_t* sm_b = smem + kStages * S::kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * S::kStageBytes);
-  uint64_t* full = bars;                   // [kStages] TMA -> MMA
-  uint64_t* empty = bars + kStages;        // [kStages] MMA -> TMA
+  uint8_t* sm_epi = smem + kStages * S::kStageBytes;  // 1024-aligned: stage sizes are multiples of 1024
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm_epi + kEpiBytes);
+  uint64_t* full = bars;                      // [kStages] TMA -> MMA
+  uint64_t* empty = bars + kStages;           // [kStages] MMA -> TMA
   uint64_t* tmem_full = bars + 2 * kStages;   // [2] MMA -> epilogue
   uint64_t* tmem_empty = tmem_full + 2;       // [2] epilogue -> MMA
   uint64_t* drain = tmem_empty + 2;           // [1] MMA completion on abort
@@ -172,13 +187,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 4);
+      mbar_init(&tmem_empty[a], kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort = 0;
     fence_barrier_init();
     tma_prefetch_map(&map_a);
     tma_prefetch_map(&map_b);
+    tma_prefetch_map(&map_out);
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -275,6 +291,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ---- epilogue: warps 2..5 cover TMEM lane quarters 2, 3, 0, 1
     const int quarter = warp & 3;
+    uint8_t* stage_base = sm_epi + (warp - 2) * 2 * kEpiBufBytes;
+    int buf = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
@@ -285,20 +303,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      const int row = m0 + quarter * 32 + lane;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const int row0 = m0 + quarter * 32;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = 0; c < BN; c += kEpiChunk) {
         float v[32];
         tmem_ld32(taddr + c, v);
-        if (row < M) epi.apply(row, n0 + c, v);
+        if (c + kEpiChunk >= BN) {
+          // Last TMEM read of this tile: hand the accumulator back to the MMA warp.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+        }
+        uint4 out[Epi::kOutBytes * 2];
+        epi.pack(n0 + c, v, out);
+        // The staging buffer must no longer be read by the store issued two steps ago.
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        uint8_t* sb = stage_base + buf * kEpiBufBytes;
+#pragma unroll
+        for (int j = 0; j < Epi::kOutBytes * 2; ++j)
+          *reinterpret_cast<uint4*>(sb + staged_offset<kRowBytes>(lane, j)) = out[j];
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          if (row0 < M) {
+            if constexpr (Epi::kReduce)
+              tma_reduce_add_2d(&map_out, sb, n0 + c, row0);
+            else
+              tma_store_2d(&map_out, sb, n0 + c, row0);
+          }
+          bulk_commit();
+        }
+        buf ^= 1;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tmem_empty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();

@@ -32,6 +32,7 @@ struct GemmArgs {
 struct GemmPlan {
   CUtensorMap map_a;
   CUtensorMap map_b;
+  CUtensorMap map_out;
   GemmArgs args;
   int bn = 0;
   int grid = 0;

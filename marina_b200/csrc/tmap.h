@@ -43,4 +43,23 @@ inline bool make_kmajor_map(CUtensorMap* map, const void* base, int elem_bytes, 
   return r == CUDA_SUCCESS;
 }
 
+// A row-major output [rows, cols] (row stride `ld` elements) written in 32 x 32 blocks whose
+// rows are 32 * elem_bytes bytes, with the matching swizzle (128, 64 or 32 bytes).
+inline bool make_store_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t rows,
+                           uint64_t cols, uint64_t ld) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * elem_bytes) % 16 != 0) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * static_cast<uint64_t>(elem_bytes)};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t estrides[2] = {1, 1};
+  const CUtensorMapSwizzle sw = elem_bytes == 4   ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : elem_bytes == 2 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                  : CU_TENSOR_MAP_SWIZZLE_32B;
+  const CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estrides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace mrn

@@ -2,11 +2,17 @@
 restatement of the reference's CPU backend, on identical encoded inputs.
 
 Tolerances (the north star's): WDL within 2e-2 absolute, legal-move priors within 3e-2
-absolute, KL(oracle || ours) < 1e-2 per position, argmax-move agreement >= 99%. The argmax
-criterion applies to the bf16-activation precisions ("bf16", "fp8w"); e4m3 activations
-("fp8", the reference's FP8 path) carry ~3.6% rms rounding noise per GEMM input, which moves
-the best move of near-uniform random-init policies on roughly one position in ten, so that
-mode is held to the WDL / prior / KL bounds and a looser argmax floor."""
+absolute, KL(oracle || ours) < 1e-2 per position, argmax-move agreement >= 99%.
+
+Argmax agreement is tie-aware: a position counts as a disagreement when the move we rank
+first has an oracle prior more than TIE (2e-4, the reference's own fp32-vs-fp32 prior
+tolerance, src/net/verify.rs:62-66) below the oracle's best. Random-init policies are close
+to uniform and a few percent of positions have top-2 prior margins below 1e-4, which no
+implementation with a different summation order can resolve; the raw agreement is printed
+beside it. The criterion applies to the bf16-activation precisions ("bf16", "fp8w"); e4m3
+activations ("fp8", the reference's FP8 path) carry ~3.6% rms rounding noise per GEMM input,
+which reorders near-uniform random-init policies on roughly one position in ten, so that mode
+is held to the WDL / prior / KL bounds and a looser argmax floor."""
 
 import threading
 
@@ -21,6 +27,7 @@ pytestmark = pytest.mark.gpu
 
 WDL_TOL, PRIOR_TOL, KL_TOL, ARGMAX_MIN = 2e-2, 3e-2, 1e-2, 0.99
 ARGMAX_MIN_FP8 = 0.80
+TIE = 2e-4
 
 
 def card(name):
@@ -35,10 +42,14 @@ def compare(priors, wdl, ref_priors, ref_wdl, counts):
     wdl_diff = float(np.abs(wdl - ref_wdl).max())
     kl = max(float(np.sum(ref_priors[p, :c] * (np.log(np.maximum(ref_priors[p, :c], 1e-30))
                                                 - np.log(np.maximum(priors[p, :c], 1e-30))))) for p, c in enumerate(counts))
-    agree = np.mean([np.argmax(priors[p, :c]) == np.argmax(ref_priors[p, :c]) for p, c in enumerate(counts)])
+    raw = np.mean([np.argmax(priors[p, :c]) == np.argmax(ref_priors[p, :c]) for p, c in enumerate(counts)])
+    agree = np.mean([ref_priors[p, np.argmax(priors[p, :c])] >= ref_priors[p, :c].max() - TIE
+                     for p, c in enumerate(counts)])
+    margins = [float(np.diff(np.sort(ref_priors[p, :c])[-2:])[0]) if c > 1 else 1.0 for p, c in enumerate(counts)]
     pad_zero = all((priors[p, c:] == 0).all() for p, c in enumerate(counts))
     sums = max(abs(float(priors[p, :c].sum()) - 1) for p, c in enumerate(counts))
-    return dict(n=n, prior=prior_diff, wdl=wdl_diff, kl=kl, argmax=float(agree), pad_zero=pad_zero, sums=sums)
+    return dict(n=n, prior=prior_diff, wdl=wdl_diff, kl=kl, argmax=float(agree), argmax_raw=float(raw),
+                oracle_margin_lt_tie=float(np.mean(np.array(margins) < TIE)), pad_zero=pad_zero, sums=sums)
 
 
 def check(m, precision):
@@ -93,6 +104,18 @@ def test_small_config_batch_256(small_setup, precision):
     ref_p, ref_w = ref if precision == "bf16" else ref_q
     net = B200Network(arch, w, max_batch=256, precision=precision)
     priors, wdl = net.evaluate_packed(boards, legal)
+    check(compare(priors, wdl, ref_p, ref_w, counts), precision)
+
+
+@pytest.mark.parametrize("net,precision", [("nano", "bf16"), ("nano", "fp8w"), ("small", "fp8w"), ("small", "fp8")])
+def test_argmax_agreement_on_1024_positions(net, precision):
+    """The argmax criterion on a sample large enough for a 1% bound to mean something."""
+    arch = card(net)
+    w = weights.random_init(arch, seed=0)
+    boards, legal, counts, _ = chess.random_positions(17, 1024, 0, 80)
+    ref_p, ref_w = oracle.OracleNetwork(arch, weights.fp8_weights(w) if precision != "bf16" else w,
+                                        threads=16).evaluate(boards, legal)
+    priors, wdl = B200Network(arch, w, max_batch=1024, precision=precision).evaluate_packed(boards, legal)
     check(compare(priors, wdl, ref_p, ref_w, counts), precision)
 
 
