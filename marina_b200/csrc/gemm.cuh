@@ -6,14 +6,15 @@
 // walks the output tiles (128 rows x BN columns) in n-fastest order, so the CTAs working on
 // the same 128-row block of A at the same time share it through L2.
 //
-// Roles (192 threads):
+// Roles (320 threads):
 //   warp 0, one lane : TMA producer. A 128x128-byte tile and a BNx128-byte tile per stage,
 //                      128-byte swizzled, into a STAGES-deep ring of shared-memory buffers.
 //   warp 1, one lane : MMA issuer. 4 tcgen05.mma (K = 32 bytes each) per stage into a TMEM
 //                      accumulator; two accumulators of BN columns alternate between tiles
 //                      so the epilogue of one tile overlaps the MMAs of the next.
-//   warps 2..5       : epilogue. Warp w reads TMEM lanes 32*(w%4).. (one output row per
-//                      thread) 32 columns at a time, applies the epilogue functor, writes the
+//   warps 2..9       : epilogue. Warp w reads TMEM lanes 32*(w%4).. (one output row per
+//                      thread) in one half of the tile's columns, 32 at a time, applies the
+//                      epilogue functor, writes the
 //                      32x32 block into a swizzled shared-memory staging buffer and one lane
 //                      issues a TMA tile store (or, for the residual stream, a TMA reduce-add),
 //                      so global writes are whole swizzle rows issued by the copy engine.
@@ -30,14 +31,14 @@
 
 namespace mrn {
 
-constexpr int kGemmThreads = 192;
+constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, each taking half of the columns
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 constexpr int kTileM = 128;
 constexpr int kStageRowBytes = 128;  // one swizzle row: 64 bf16 or 128 e4m3 values of K
 constexpr uint32_t kTmemCols = 512;  // two accumulators of up to 256 f32 columns
-constexpr int kEpiWarps = 4;
 constexpr int kEpiChunk = 32;                       // columns per epilogue step
 constexpr int kEpiBufBytes = 32 * kEpiChunk * 4;    // one 32x32 staging block at up to 4 B
-constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;  // double-buffered per warp
+constexpr int kEpiBytes = kEpiWarps * kEpiBufBytes;  // one staging block per epilogue warp
 constexpr int kMaxSmem = 232448;                    // 227 KB per CTA
 
 template <int BN>
@@ -53,7 +54,17 @@ struct GemmShape {
   static constexpr int kSmemBytes = 1024 /*alignment slack*/ + kStages * kStageBytes + kEpiBytes + kBarrierBytes;
 };
 
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752f)); }
+// GELU(x) = 0.5 x (1 + erf(x / sqrt 2)) with erf from Abramowitz & Stegun 7.1.26
+// (|error| <= 1.5e-7, the approximation the reference's CPU backend uses,
+// src/net/cpu.rs:284-302), evaluated with the hardware reciprocal and exponential.
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;
+  const float t = __fdividef(1.f, fmaf(0.3275911f, z, 1.f));
+  const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f),
+                              0.254829592f);
+  const float e = 1.f - poly * __expf(-z * z);
+  return 0.5f * x * (1.f + copysignf(e, x));
+}
 
 // Byte offset of 16-byte chunk `j` of row `r` in a staging block whose rows are RB bytes and
 // which the TMA map reads with the matching swizzle (RB 128 -> 128B, 64 -> 64B, 32 -> 32B):
@@ -289,10 +300,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ---- epilogue: warps 2..5 cover TMEM lane quarters 2, 3, 0, 1
+    // ---- epilogue: warps 2..9; warp w reads TMEM lane quarter w % 4 and one half of the
+    // tile's columns
     const int quarter = warp & 3;
-    uint8_t* stage_base = sm_epi + (warp - 2) * 2 * kEpiBufBytes;
-    int buf = 0;
+    const int half = (warp - 2) >> 2;
+    constexpr int kHalf = BN / 2;
+    uint8_t* sb = sm_epi + (warp - 2) * kEpiBufBytes;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
@@ -306,21 +319,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int row0 = m0 + quarter * 32;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += kEpiChunk) {
+      for (int c = half * kHalf; c < (half + 1) * kHalf; c += kEpiChunk) {
         float v[32];
         tmem_ld32(taddr + c, v);
-        if (c + kEpiChunk >= BN) {
-          // Last TMEM read of this tile: hand the accumulator back to the MMA warp.
+        if (c + kEpiChunk >= (half + 1) * kHalf) {
+          // Last TMEM read of this tile by this warp: hand the accumulator back.
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tmem_empty[acc]);
         }
         uint4 out[Epi::kOutBytes * 2];
         epi.pack(n0 + c, v, out);
-        // The staging buffer must no longer be read by the store issued two steps ago.
-        if (lane == 0) bulk_wait_read<1>();
+        // The staging block must no longer be read by this warp's previous store.
+        if (lane == 0) bulk_wait_read<0>();
         __syncwarp();
-        uint8_t* sb = stage_base + buf * kEpiBufBytes;
 #pragma unroll
         for (int j = 0; j < Epi::kOutBytes * 2; ++j)
           *reinterpret_cast<uint4*>(sb + staged_offset<kRowBytes>(lane, j)) = out[j];
@@ -335,7 +347,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           bulk_commit();
         }
-        buf ^= 1;
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
