@@ -154,20 +154,30 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedParams e, NormParams
 }
 
 // ---- LayerNorm, one warp per row (src/net/cpu.rs:323-343) --------------------------------
+// Warps stride over rows; the next row's loads are issued before the current row's
+// reductions so every warp keeps a row of reads in flight.
 template <int VPL, int VEC>
 __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, NormParams n, int rows, int d) {
   const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int stride = gridDim.x * 8;
+  int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
-  WarpRow<VPL, VEC> r;
-  r.load(x + static_cast<size_t>(row) * d, lane);
-  r.layernorm(n.gamma, n.beta, n.eps, d, lane);
-  const size_t off = static_cast<size_t>(row) * d * (n.out_type == ActType::kBf16 ? 2 : 1);
-  r.store_act(static_cast<uint8_t*>(n.out) + off, n.out_type, n.inv_q, lane);
+  const size_t out_bytes = n.out_type == ActType::kBf16 ? 2 : 1;
+  WarpRow<VPL, VEC> cur, nxt;
+  cur.load(x + static_cast<size_t>(row) * d, lane);
+  for (;;) {
+    const int next = row + stride;
+    if (next < rows) nxt.load(x + static_cast<size_t>(next) * d, lane);
+    cur.layernorm(n.gamma, n.beta, n.eps, d, lane);
+    cur.store_act(static_cast<uint8_t*>(n.out) + static_cast<size_t>(row) * d * out_bytes, n.out_type, n.inv_q, lane);
+    if (next >= rows) break;
+    row = next;
+    cur = nxt;
+  }
 }
 
 // ---- attention ---------------------------------------------------------------------------
-// One CTA per (position, head); Q, K and V of the head (t <= 80 rows, zero-padded to 80) live
+// Work item = (position, head); Q, K and V of the item (t <= 80 rows, zero-padded to 80) live
 // in shared memory. Warp w owns query rows 16w..16w+15: S = Q K^T for its strip stays in
 // registers (mma.sync m16n8k16, f32 accumulation), the softmax runs on the accumulators with
 // quad shuffles, and the probabilities feed P V straight from registers.
@@ -195,129 +205,161 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 constexpr int kAttnRows = 80;
 constexpr int kAttnWarps = kAttnRows / 16;
+constexpr int kAttnCtasPerSm = 3;
 
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(a), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Persistent: each CTA walks (position, head) items with a stride of the grid, keeping two
+// Q/K/V buffers so the next item's loads (cp.async) overlap the current item's math. Rows
+// t..79 of both buffers are zeroed once and never written again.
 template <int HD>
-__global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(AttentionParams p) {
+__global__ void __launch_bounds__(kAttnWarps * 32, kAttnCtasPerSm) attention_kernel(AttentionParams p, int items) {
   constexpr int LD = HD + 8;  // bf16 elements per staged row (16-byte multiple, conflict-free)
   constexpr int CH = HD / 8;  // 16-byte chunks per row
-  __shared__ __align__(16) __nv_bfloat16 sq[kAttnRows * LD];
-  __shared__ __align__(16) __nv_bfloat16 sk[kAttnRows * LD];
-  __shared__ __align__(16) __nv_bfloat16 sv[kAttnRows * LD];
+  constexpr int MAT = kAttnRows * LD;
+  extern __shared__ __align__(16) __nv_bfloat16 smem_attn[];  // [2][3][kAttnRows][LD]
 
-  const int t = p.t, d = p.d;
-  const int pos = blockIdx.x / p.heads;
-  const int head = blockIdx.x - pos * p.heads;
-  const __nv_bfloat16* base =
-      static_cast<const __nv_bfloat16*>(p.qkv) + static_cast<size_t>(pos) * t * 3 * d + head * HD;
-  for (int i = threadIdx.x; i < kAttnRows * CH; i += blockDim.x) {
-    const int row = i / CH, ch = i - row * CH;
-    uint4 q = make_uint4(0, 0, 0, 0), k = q, v = q;
-    if (row < t) {
-      const __nv_bfloat16* r = base + static_cast<size_t>(row) * 3 * d + ch * 8;
-      q = *reinterpret_cast<const uint4*>(r);
-      k = *reinterpret_cast<const uint4*>(r + d);
-      v = *reinterpret_cast<const uint4*>(r + 2 * d);
-    }
-    *reinterpret_cast<uint4*>(sq + row * LD + ch * 8) = q;
-    *reinterpret_cast<uint4*>(sk + row * LD + ch * 8) = k;
-    *reinterpret_cast<uint4*>(sv + row * LD + ch * 8) = v;
-  }
-  __syncthreads();
-
+  const int t = p.t, d = p.d, heads = p.heads;
+  const __nv_bfloat16* qkv = static_cast<const __nv_bfloat16*>(p.qkv);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
   const int r0 = warp * 16;
-  if (r0 >= t) return;
 
-  // S = Q K^T for rows r0..r0+15 against all 80 (padded) keys.
-  float s[10][4];
-#pragma unroll
-  for (int nt = 0; nt < 10; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-#pragma unroll
-  for (int kk = 0; kk < HD; kk += 16) {
-    uint32_t a[4];
-    a[0] = lds32(sq + (r0 + g) * LD + kk + 2 * tq);
-    a[1] = lds32(sq + (r0 + g + 8) * LD + kk + 2 * tq);
-    a[2] = lds32(sq + (r0 + g) * LD + kk + 8 + 2 * tq);
-    a[3] = lds32(sq + (r0 + g + 8) * LD + kk + 8 + 2 * tq);
-#pragma unroll
-    for (int nt = 0; nt < 10; ++nt) {
-      const __nv_bfloat16* kr = sk + (nt * 8 + g) * LD + kk + 2 * tq;
-      mma_16816(s[nt], a, lds32(kr), lds32(kr + 8));
-    }
+  for (int i = threadIdx.x; i < 2 * 3 * (kAttnRows - t) * CH; i += blockDim.x) {
+    const int per_mat = (kAttnRows - t) * CH;
+    const int m = i / per_mat, rem = i - m * per_mat;
+    const int row = t + rem / CH, ch = rem % CH;
+    *reinterpret_cast<uint4*>(smem_attn + m * MAT + row * LD + ch * 8) = make_uint4(0, 0, 0, 0);
   }
 
-  // Softmax of rows g (values 0,1) and g+8 (values 2,3) of the strip; keys >= t are masked.
+  auto load = [&](int item, int buf) {
+    const int pos = item / heads, head = item - pos * heads;
+    const __nv_bfloat16* base = qkv + static_cast<size_t>(pos) * t * 3 * d + head * HD;
+    __nv_bfloat16* dst = smem_attn + buf * 3 * MAT;
+    for (int i = threadIdx.x; i < t * CH * 3; i += blockDim.x) {
+      const int m = i / (t * CH), rem = i - m * (t * CH);
+      const int row = rem / CH, ch = rem - row * CH;
+      cp_async16(dst + m * MAT + row * LD + ch * 8, base + static_cast<size_t>(row) * 3 * d + m * d + ch * 8);
+    }
+  };
+
+  int item = blockIdx.x;
+  if (item < items) load(item, 0);
+  cp_async_commit();
   const float scale_log2 = rsqrtf(static_cast<float>(HD)) * 1.4426950408889634f;
-  float m0 = -INFINITY, m1 = -INFINITY;
-#pragma unroll
-  for (int nt = 0; nt < 10; ++nt)
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-      if (nt * 8 + 2 * tq + j < t) {
-        m0 = fmaxf(m0, s[nt][j]);
-        m1 = fmaxf(m1, s[nt][2 + j]);
-      }
-  m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
-  m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
-  m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
-  m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
-  float l0 = 0.f, l1 = 0.f;
-#pragma unroll
-  for (int nt = 0; nt < 10; ++nt)
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const bool valid = nt * 8 + 2 * tq + j < t;
-      s[nt][j] = valid ? exp2f((s[nt][j] - m0) * scale_log2) : 0.f;
-      s[nt][2 + j] = valid ? exp2f((s[nt][2 + j] - m1) * scale_log2) : 0.f;
-      l0 += s[nt][j];
-      l1 += s[nt][2 + j];
-    }
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  for (int it = 0; item < items; ++it, item += gridDim.x) {
+    const int buf = it & 1;
+    const int next = item + gridDim.x;
+    if (next < items) load(next, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
 
-  // O = P V: P comes from the S accumulators (two n-tiles make one k16 A fragment).
-  float o[HD / 8][4];
+    const __nv_bfloat16* sq = smem_attn + buf * 3 * MAT;
+    const __nv_bfloat16* sk = sq + MAT;
+    const __nv_bfloat16* sv = sk + MAT;
+    const int pos = item / heads, head = item - pos * heads;
+    if (r0 < t) {
+      // S = Q K^T for rows r0..r0+15 against all 80 (padded) keys.
+      float s[10][4];
 #pragma unroll
-  for (int nt = 0; nt < HD / 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+      for (int nt = 0; nt < 10; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
 #pragma unroll
-  for (int kk = 0; kk < 5; ++kk) {
-    uint32_t a[4];
-    a[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-    a[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-    a[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-    a[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-    const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      for (int kk = 0; kk < HD; kk += 16) {
+        uint32_t a[4];
+        a[0] = lds32(sq + (r0 + g) * LD + kk + 2 * tq);
+        a[1] = lds32(sq + (r0 + g + 8) * LD + kk + 2 * tq);
+        a[2] = lds32(sq + (r0 + g) * LD + kk + 8 + 2 * tq);
+        a[3] = lds32(sq + (r0 + g + 8) * LD + kk + 8 + 2 * tq);
 #pragma unroll
-    for (int nt = 0; nt < HD / 8; nt += 2) {
-      uint32_t b[4];
-      ldmatrix_x4_trans(b, sv + key * LD + nt * 8 + ((lane >> 4) & 1) * 8);
-      mma_16816(o[nt], a, b[0], b[1]);
-      mma_16816(o[nt + 1], a, b[2], b[3]);
-    }
-  }
+        for (int nt = 0; nt < 10; ++nt) {
+          const __nv_bfloat16* kr = sk + (nt * 8 + g) * LD + kk + 2 * tq;
+          mma_16816(s[nt], a, lds32(kr), lds32(kr + 8));
+        }
+      }
+      // Softmax of rows g (values 0,1) and g+8 (values 2,3); keys >= t are masked.
+      float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 10; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          if (nt * 8 + 2 * tq + j < t) {
+            m0 = fmaxf(m0, s[nt][j]);
+            m1 = fmaxf(m1, s[nt][2 + j]);
+          }
+      m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
+      m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
+      m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+      m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
+      float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 10; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const bool valid = nt * 8 + 2 * tq + j < t;
+          s[nt][j] = valid ? exp2f((s[nt][j] - m0) * scale_log2) : 0.f;
+          s[nt][2 + j] = valid ? exp2f((s[nt][2 + j] - m1) * scale_log2) : 0.f;
+          l0 += s[nt][j];
+          l1 += s[nt][2 + j];
+        }
+      l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+      l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
 
-  const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+      // O = P V: P comes from the S accumulators (two n-tiles make one k16 A fragment).
+      float o[HD / 8][4];
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    const int row = r0 + g + half * 8;
-    if (row >= t) continue;
-    const float inv = half ? inv1 : inv0;
-    const size_t at = (static_cast<size_t>(pos) * t + row) * d + head * HD + 2 * tq;
+      for (int nt = 0; nt < HD / 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
 #pragma unroll
-    for (int nt = 0; nt < HD / 8; ++nt) {
-      const float v0 = o[nt][2 * half] * inv, v1 = o[nt][2 * half + 1] * inv;
-      if (p.out_type == ActType::kBf16) {
-        *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.out) + at + nt * 8) =
-            __floats2bfloat162_rn(v0, v1);
-      } else {
-        *reinterpret_cast<__nv_fp8x2_storage_t*>(static_cast<uint8_t*>(p.out) + at + nt * 8) =
-            __nv_cvt_float2_to_fp8x2(make_float2(v0 * p.inv_q, v1 * p.inv_q), __NV_SATFINITE, __NV_E4M3);
+      for (int kk = 0; kk < 5; ++kk) {
+        uint32_t a[4];
+        a[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+        a[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+        a[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        a[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+        const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+        for (int nt = 0; nt < HD / 8; nt += 2) {
+          uint32_t b[4];
+          ldmatrix_x4_trans(b, sv + key * LD + nt * 8 + ((lane >> 4) & 1) * 8);
+          mma_16816(o[nt], a, b[0], b[1]);
+          mma_16816(o[nt + 1], a, b[2], b[3]);
+        }
+      }
+
+      const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int row = r0 + g + half * 8;
+        if (row >= t) continue;
+        const float inv = half ? inv1 : inv0;
+        const size_t at = (static_cast<size_t>(pos) * t + row) * d + head * HD + 2 * tq;
+#pragma unroll
+        for (int nt = 0; nt < HD / 8; ++nt) {
+          const float v0 = o[nt][2 * half] * inv, v1 = o[nt][2 * half + 1] * inv;
+          if (p.out_type == ActType::kBf16) {
+            *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.out) + at + nt * 8) =
+                __floats2bfloat162_rn(v0, v1);
+          } else {
+            *reinterpret_cast<__nv_fp8x2_storage_t*>(static_cast<uint8_t*>(p.out) + at + nt * 8) =
+                __nv_cvt_float2_to_fp8x2(make_float2(v0 * p.inv_q, v1 * p.inv_q), __NV_SATFINITE, __NV_E4M3);
+          }
+        }
       }
     }
+    // Every warp is done with `buf` before the load two items ahead overwrites it.
+    __syncthreads();
   }
+  cp_async_wait<0>();
 }
 
 // ---- heads -----------------------------------------------------------------------------
@@ -465,7 +507,12 @@ struct EmbedLaunch {
 template <int VPL, int VEC>
 struct NormLaunch {
   static cudaError_t run(int d, const float* x, const NormParams& n, int rows, cudaStream_t s) {
-    layernorm_kernel<VPL, VEC><<<(rows + 7) / 8, 256, 0, s>>>(x, n, rows, d);
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int blocks_needed = (rows + 7) / 8;
+    const int grid = blocks_needed < sms * 8 ? blocks_needed : sms * 8;
+    layernorm_kernel<VPL, VEC><<<grid, 256, 0, s>>>(x, n, rows, d);
     return cudaGetLastError();
   }
 };
@@ -498,15 +545,30 @@ cudaError_t launch_layernorm(const float* x, const NormParams& n, int rows, int 
 }
 
 cudaError_t launch_attention(const AttentionParams& p, int positions, int head_dim, cudaStream_t s) {
-  if (p.t > kAttnRows) return cudaErrorInvalidValue;
-  const int blocks = positions * p.heads;
-  if (head_dim == 64)
-    attention_kernel<64><<<blocks, kAttnWarps * 32, 0, s>>>(p);
-  else if (head_dim == 32)
-    attention_kernel<32><<<blocks, kAttnWarps * 32, 0, s>>>(p);
-  else
+  if (p.t > kAttnRows || p.t < 1) return cudaErrorInvalidValue;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int items = positions * p.heads;
+  const int grid = items < sms * kAttnCtasPerSm ? items : sms * kAttnCtasPerSm;
+  if (head_dim == 64) {
+    const size_t smem = 2 * 3 * kAttnRows * (64 + 8) * sizeof(__nv_bfloat16);
+    attention_kernel<64><<<grid, kAttnWarps * 32, smem, s>>>(p, items);
+  } else if (head_dim == 32) {
+    const size_t smem = 2 * 3 * kAttnRows * (32 + 8) * sizeof(__nv_bfloat16);
+    attention_kernel<32><<<grid, kAttnWarps * 32, smem, s>>>(p, items);
+  } else {
     return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
+}
+
+cudaError_t prepare_attention() {
+  cudaError_t e = cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       2 * 3 * kAttnRows * (64 + 8) * 2);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(attention_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              2 * 3 * kAttnRows * (32 + 8) * 2);
 }
 
 cudaError_t launch_heads(const HeadsParams& p, int positions, int d, cudaStream_t s) {

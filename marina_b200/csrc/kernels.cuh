@@ -45,6 +45,8 @@ struct AttentionParams {
   int t, d, heads;
 };
 cudaError_t launch_attention(const AttentionParams& p, int positions, int head_dim, cudaStream_t s);
+// Opt the attention kernels into their dynamic shared memory (once per device).
+cudaError_t prepare_attention();
 
 struct HeadsParams {
   const float* x;             // [R, d] residual stream after the last layer

@@ -568,7 +568,8 @@ MRN_API int mrn_create(const mrn_arch* arch, const mrn_weights* weights, int dev
     return bail(c->fail(MRN_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", device, prop.major, prop.minor));
   if (cudaSetDevice(device) != cudaSuccess) return bail(c->fail(MRN_ERR_CUDA, "cudaSetDevice(%d) failed", device));
   c->num_sms = prop.multiProcessorCount;
-  if (mrn::gemm_prepare_device() != cudaSuccess) return bail(c->fail(MRN_ERR_CUDA, "GEMM kernel attributes"));
+  if (mrn::gemm_prepare_device() != cudaSuccess || mrn::prepare_attention() != cudaSuccess)
+    return bail(c->fail(MRN_ERR_CUDA, "kernel shared-memory attributes"));
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(c->fail(MRN_ERR_CUDA, "cudaStreamCreate failed"));
 
