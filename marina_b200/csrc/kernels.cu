@@ -79,6 +79,20 @@ struct WarpRow {
     }
   }
 
+  // The same with gamma and beta already in registers (same element layout as this row).
+  __device__ __forceinline__ void layernorm_regs(const WarpRow& g, const WarpRow& b, float eps, int d) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) s += v[i];
+    const float mean = warp_sum(s) / static_cast<float>(d);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) q += (v[i] - mean) * (v[i] - mean);
+    const float inv = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(d) + eps);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) v[i] = (v[i] - mean) * inv * g.v[i] + b.v[i];
+  }
+
   __device__ __forceinline__ void store_act(void* dst, ActType type, float inv_q, int lane) const {
 #pragma unroll
     for (int c = 0; c < kChunks; ++c) {
@@ -154,8 +168,8 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedParams e, NormParams
 }
 
 // ---- LayerNorm, one warp per row (src/net/cpu.rs:323-343) --------------------------------
-// Warps stride over rows; the next row's loads are issued before the current row's
-// reductions so every warp keeps a row of reads in flight.
+// Warps stride over rows with gamma/beta held in registers; the next row's loads are issued
+// before the current row's reductions so every warp keeps a row of reads in flight.
 template <int VPL, int VEC>
 __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, NormParams n, int rows, int d) {
   const int lane = threadIdx.x & 31;
@@ -163,12 +177,15 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
   int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
   const size_t out_bytes = n.out_type == ActType::kBf16 ? 2 : 1;
-  WarpRow<VPL, VEC> cur, nxt;
+  using Row = WarpRow<VPL, VEC>;
+  Row gamma, beta, cur, nxt;
+  gamma.load(n.gamma, lane);
+  beta.load(n.beta, lane);
   cur.load(x + static_cast<size_t>(row) * d, lane);
   for (;;) {
     const int next = row + stride;
     if (next < rows) nxt.load(x + static_cast<size_t>(next) * d, lane);
-    cur.layernorm(n.gamma, n.beta, n.eps, d, lane);
+    cur.layernorm_regs(gamma, beta, n.eps, d);
     cur.store_act(static_cast<uint8_t*>(n.out) + static_cast<size_t>(row) * d * out_bytes, n.out_type, n.inv_q, lane);
     if (next >= rows) break;
     row = next;
