@@ -234,38 +234,52 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // Persistent: each CTA walks (position, head) items with a stride of the grid, keeping two
 // Q/K/V buffers so the next item's loads (cp.async) overlap the current item's math. Rows
-// t..79 of both buffers are zeroed once and never written again.
-template <int HD>
+// T..79 of both buffers are zeroed once and never written again. T (tokens per position) is a
+// template parameter so the key masks fold to constants: key tiles entirely past T are skipped.
+// Each warp writes its normalised 16-row output strip over its own (dead) Q rows in shared
+// memory and stores it with 16-byte writes.
+template <int HD, int T, bool E4M3>
 __global__ void __launch_bounds__(kAttnWarps * 32, kAttnCtasPerSm) attention_kernel(AttentionParams p, int items) {
   constexpr int LD = HD + 8;  // bf16 elements per staged row (16-byte multiple, conflict-free)
   constexpr int CH = HD / 8;  // 16-byte chunks per row
   constexpr int MAT = kAttnRows * LD;
+  constexpr int NT = (T + 7) / 8;    // key tiles of 8 holding at least one valid key
+  constexpr int KS = (T + 15) / 16;  // k16 steps of P V
+  constexpr int ROWS_PER_PASS = kAttnWarps * 32 / CH;
+  static_assert(T <= kAttnRows && 2 * KS <= 10, "tokens per position");
   extern __shared__ __align__(16) __nv_bfloat16 smem_attn[];  // [2][3][kAttnRows][LD]
 
-  const int t = p.t, d = p.d, heads = p.heads;
+  const int d = p.d, heads = p.heads;
   const __nv_bfloat16* qkv = static_cast<const __nv_bfloat16*>(p.qkv);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
   const int r0 = warp * 16;
 
-  for (int i = threadIdx.x; i < 2 * 3 * (kAttnRows - t) * CH; i += blockDim.x) {
-    const int per_mat = (kAttnRows - t) * CH;
+  for (int i = threadIdx.x; i < 2 * 3 * (kAttnRows - T) * CH; i += blockDim.x) {
+    const int per_mat = (kAttnRows - T) * CH;
     const int m = i / per_mat, rem = i - m * per_mat;
-    const int row = t + rem / CH, ch = rem % CH;
+    const int row = T + rem / CH, ch = rem % CH;
     *reinterpret_cast<uint4*>(smem_attn + m * MAT + row * LD + ch * 8) = make_uint4(0, 0, 0, 0);
   }
 
+  const int ld_ch = threadIdx.x % CH, ld_row0 = threadIdx.x / CH;
   auto load = [&](int item, int buf) {
     const int pos = item / heads, head = item - pos * heads;
-    const __nv_bfloat16* base = qkv + static_cast<size_t>(pos) * t * 3 * d + head * HD;
-    __nv_bfloat16* dst = smem_attn + buf * 3 * MAT;
-    for (int i = threadIdx.x; i < t * CH * 3; i += blockDim.x) {
-      const int m = i / (t * CH), rem = i - m * (t * CH);
-      const int row = rem / CH, ch = rem - row * CH;
-      cp_async16(dst + m * MAT + row * LD + ch * 8, base + static_cast<size_t>(row) * 3 * d + m * d + ch * 8);
-    }
+    const __nv_bfloat16* base = qkv + static_cast<size_t>(pos) * T * 3 * d + head * HD + ld_ch * 8;
+    __nv_bfloat16* dst = smem_attn + buf * 3 * MAT + ld_ch * 8;
+#pragma unroll
+    for (int m = 0; m < 3; ++m)
+#pragma unroll
+      for (int row = ld_row0; row < T; row += ROWS_PER_PASS)
+        cp_async16(dst + m * MAT + row * LD, base + static_cast<size_t>(row) * 3 * d + m * d);
   };
 
   int item = blockIdx.x;
@@ -280,15 +294,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32, kAttnCtasPerSm) attention_ker
     cp_async_wait<1>();
     __syncthreads();
 
-    const __nv_bfloat16* sq = smem_attn + buf * 3 * MAT;
+    __nv_bfloat16* sq = smem_attn + buf * 3 * MAT;
     const __nv_bfloat16* sk = sq + MAT;
     const __nv_bfloat16* sv = sk + MAT;
     const int pos = item / heads, head = item - pos * heads;
-    if (r0 < t) {
-      // S = Q K^T for rows r0..r0+15 against all 80 (padded) keys.
-      float s[10][4];
+    if (r0 < T) {
+      // S = Q K^T for rows r0..r0+15 against the key tiles holding valid keys.
+      float s[2 * KS][4];
 #pragma unroll
-      for (int nt = 0; nt < 10; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      for (int nt = 0; nt < 2 * KS; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
 #pragma unroll
       for (int kk = 0; kk < HD; kk += 16) {
         uint32_t a[4];
@@ -297,18 +311,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32, kAttnCtasPerSm) attention_ker
         a[2] = lds32(sq + (r0 + g) * LD + kk + 8 + 2 * tq);
         a[3] = lds32(sq + (r0 + g + 8) * LD + kk + 8 + 2 * tq);
 #pragma unroll
-        for (int nt = 0; nt < 10; ++nt) {
+        for (int nt = 0; nt < NT; ++nt) {
           const __nv_bfloat16* kr = sk + (nt * 8 + g) * LD + kk + 2 * tq;
           mma_16816(s[nt], a, lds32(kr), lds32(kr + 8));
         }
       }
-      // Softmax of rows g (values 0,1) and g+8 (values 2,3); keys >= t are masked.
+      // Softmax of rows g (values 0,1) and g+8 (values 2,3); keys >= T are masked.
       float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-      for (int nt = 0; nt < 10; ++nt)
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int j = 0; j < 2; ++j)
-          if (nt * 8 + 2 * tq + j < t) {
+          if (nt * 8 + 7 < T || nt * 8 + 2 * tq + j < T) {
             m0 = fmaxf(m0, s[nt][j]);
             m1 = fmaxf(m1, s[nt][2 + j]);
           }
@@ -316,14 +330,20 @@ __global__ void __launch_bounds__(kAttnWarps * 32, kAttnCtasPerSm) attention_ker
       m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
       m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
       m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
+      const float b0 = -m0 * scale_log2, b1 = -m1 * scale_log2;
       float l0 = 0.f, l1 = 0.f;
 #pragma unroll
-      for (int nt = 0; nt < 10; ++nt)
+      for (int nt = 0; nt < 2 * KS; ++nt)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-          const bool valid = nt * 8 + 2 * tq + j < t;
-          s[nt][j] = valid ? exp2f((s[nt][j] - m0) * scale_log2) : 0.f;
-          s[nt][2 + j] = valid ? exp2f((s[nt][2 + j] - m1) * scale_log2) : 0.f;
+          if (nt >= NT) {
+            s[nt][j] = s[nt][2 + j] = 0.f;
+          } else if (nt * 8 + 7 < T || nt * 8 + 2 * tq + j < T) {
+            s[nt][j] = ex2_approx(fmaf(s[nt][j], scale_log2, b0));
+            s[nt][2 + j] = ex2_approx(fmaf(s[nt][2 + j], scale_log2, b1));
+          } else {
+            s[nt][j] = s[nt][2 + j] = 0.f;
+          }
           l0 += s[nt][j];
           l1 += s[nt][2 + j];
         }
@@ -337,7 +357,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, kAttnCtasPerSm) attention_ker
 #pragma unroll
       for (int nt = 0; nt < HD / 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
 #pragma unroll
-      for (int kk = 0; kk < 5; ++kk) {
+      for (int kk = 0; kk < KS; ++kk) {
         uint32_t a[4];
         a[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
         a[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
@@ -353,24 +373,35 @@ __global__ void __launch_bounds__(kAttnWarps * 32, kAttnCtasPerSm) attention_ker
         }
       }
 
+      // Normalised strip -> this warp's Q rows (no longer read) -> 16-byte global stores.
       const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+      __syncwarp();
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int row = r0 + g + half * 8;
-        if (row >= t) continue;
-        const float inv = half ? inv1 : inv0;
-        const size_t at = (static_cast<size_t>(pos) * t + row) * d + head * HD + 2 * tq;
-#pragma unroll
-        for (int nt = 0; nt < HD / 8; ++nt) {
-          const float v0 = o[nt][2 * half] * inv, v1 = o[nt][2 * half + 1] * inv;
-          if (p.out_type == ActType::kBf16) {
-            *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.out) + at + nt * 8) =
-                __floats2bfloat162_rn(v0, v1);
-          } else {
-            *reinterpret_cast<__nv_fp8x2_storage_t*>(static_cast<uint8_t*>(p.out) + at + nt * 8) =
-                __nv_cvt_float2_to_fp8x2(make_float2(v0 * p.inv_q, v1 * p.inv_q), __NV_SATFINITE, __NV_E4M3);
-          }
+      for (int nt = 0; nt < HD / 8; ++nt) {
+        const int col = nt * 8 + 2 * tq;
+        if constexpr (E4M3) {
+          uint8_t* so = reinterpret_cast<uint8_t*>(sq);
+          *reinterpret_cast<__nv_fp8x2_storage_t*>(so + (r0 + g) * (LD * 2) + col) = __nv_cvt_float2_to_fp8x2(
+              make_float2(o[nt][0] * inv0 * p.inv_q, o[nt][1] * inv0 * p.inv_q), __NV_SATFINITE, __NV_E4M3);
+          *reinterpret_cast<__nv_fp8x2_storage_t*>(so + (r0 + g + 8) * (LD * 2) + col) = __nv_cvt_float2_to_fp8x2(
+              make_float2(o[nt][2] * inv1 * p.inv_q, o[nt][3] * inv1 * p.inv_q), __NV_SATFINITE, __NV_E4M3);
+        } else {
+          *reinterpret_cast<__nv_bfloat162*>(sq + (r0 + g) * LD + col) = __floats2bfloat162_rn(o[nt][0] * inv0, o[nt][1] * inv0);
+          *reinterpret_cast<__nv_bfloat162*>(sq + (r0 + g + 8) * LD + col) =
+              __floats2bfloat162_rn(o[nt][2] * inv1, o[nt][3] * inv1);
         }
+      }
+      __syncwarp();
+      constexpr int kRowBytes = HD * (E4M3 ? 1 : 2);
+      constexpr int kChunks = kRowBytes / 16;  // 16-byte chunks per output row
+      for (int i = lane; i < 16 * kChunks; i += 32) {
+        const int rr = i / kChunks, c = i - rr * kChunks;
+        const int row = r0 + rr;
+        if (row >= T) continue;
+        const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(sq) + row * (LD * 2) + c * 16);
+        uint8_t* dst = static_cast<uint8_t*>(p.out) +
+                       ((static_cast<size_t>(pos) * T + row) * d + head * HD) * (E4M3 ? 1 : 2) + c * 16;
+        *reinterpret_cast<uint4*>(dst) = v;
       }
     }
     // Every warp is done with `buf` before the load two items ahead overwrites it.
@@ -561,31 +592,43 @@ cudaError_t launch_layernorm(const float* x, const NormParams& n, int rows, int 
   return dispatch_d<NormLaunch>(d, x, n, rows, s);
 }
 
+namespace {
+template <int HD, int T>
+cudaError_t launch_attention_t(const AttentionParams& p, int grid, int items, cudaStream_t s) {
+  const size_t smem = 2 * 3 * kAttnRows * (HD + 8) * sizeof(__nv_bfloat16);
+  if (p.out_type == ActType::kE4m3)
+    attention_kernel<HD, T, true><<<grid, kAttnWarps * 32, smem, s>>>(p, items);
+  else
+    attention_kernel<HD, T, false><<<grid, kAttnWarps * 32, smem, s>>>(p, items);
+  return cudaGetLastError();
+}
+
+template <int HD, int T>
+cudaError_t prepare_attention_t() {
+  const int smem = 2 * 3 * kAttnRows * (HD + 8) * 2;
+  cudaError_t e = cudaFuncSetAttribute(attention_kernel<HD, T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(attention_kernel<HD, T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+}  // namespace
+
+// Board mode has 65 tokens (one state token, 64 squares; src/net/model.rs:17).
 cudaError_t launch_attention(const AttentionParams& p, int positions, int head_dim, cudaStream_t s) {
-  if (p.t > kAttnRows || p.t < 1) return cudaErrorInvalidValue;
+  if (p.t != 65) return cudaErrorInvalidValue;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int items = positions * p.heads;
   const int grid = items < sms * kAttnCtasPerSm ? items : sms * kAttnCtasPerSm;
-  if (head_dim == 64) {
-    const size_t smem = 2 * 3 * kAttnRows * (64 + 8) * sizeof(__nv_bfloat16);
-    attention_kernel<64><<<grid, kAttnWarps * 32, smem, s>>>(p, items);
-  } else if (head_dim == 32) {
-    const size_t smem = 2 * 3 * kAttnRows * (32 + 8) * sizeof(__nv_bfloat16);
-    attention_kernel<32><<<grid, kAttnWarps * 32, smem, s>>>(p, items);
-  } else {
-    return cudaErrorInvalidValue;
-  }
-  return cudaGetLastError();
+  if (head_dim == 64) return launch_attention_t<64, 65>(p, grid, items, s);
+  if (head_dim == 32) return launch_attention_t<32, 65>(p, grid, items, s);
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t prepare_attention() {
-  cudaError_t e = cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       2 * 3 * kAttnRows * (64 + 8) * 2);
+  cudaError_t e = prepare_attention_t<64, 65>();
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(attention_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              2 * 3 * kAttnRows * (32 + 8) * 2);
+  return prepare_attention_t<32, 65>();
 }
 
 cudaError_t launch_heads(const HeadsParams& p, int positions, int d, cudaStream_t s) {

@@ -27,7 +27,7 @@ using mrn::GemmPlan;
 
 constexpr float kE4m3Max = 448.f;  // largest finite e4m3 (src/net/cuda/mod.rs:86-87)
 constexpr float kFp8Margin = 1.25f;  // headroom over the calibration maxima (:83-85)
-constexpr int kMaxTokens = 80;
+constexpr int kTokens = 65;  // board mode: one state token, 64 squares (src/net/model.rs:17)
 
 thread_local std::string g_create_error;
 
@@ -543,7 +543,8 @@ MRN_API int mrn_create(const mrn_arch* arch, const mrn_weights* weights, int dev
   if (!width_ok || c->dff % 64 != 0)
     return bail(c->fail(MRN_ERR_UNSUPPORTED, "d_model %d / d_ff %d: d_model in {64..512 step 64, 640, 768, 1024}, d_ff a multiple of 64",
                         c->d, c->dff));
-  if (c->t > kMaxTokens) return bail(c->fail(MRN_ERR_UNSUPPORTED, "%d tokens per position (at most %d)", c->t, kMaxTokens));
+  if (c->t != kTokens)
+    return bail(c->fail(MRN_ERR_UNSUPPORTED, "%d tokens per position (the kernels are built for %d)", c->t, kTokens));
   if (c->gelu != MRN_GELU_ERF) return bail(c->fail(MRN_ERR_UNSUPPORTED, "only the erf GELU is implemented"));
   if (precision == MRN_PRECISION_FP8) {
     if (!arch->fp8_amax)
