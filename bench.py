@@ -134,6 +134,18 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def reduce_max(v: float, world: int, device) -> float:
+    """The maximum of `v` over all ranks of the default process group (identity when alone)."""
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 # ---- clocks during the timed region ---------------------------------------------------------
 class ClockSampler:
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
@@ -209,11 +221,7 @@ def run_ours(args):
             dist.barrier()
 
     def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return reduce_max(v, world, dev)
 
     arch, w = load_net(args.net)
     B = args.batch
