@@ -9,9 +9,12 @@ namespace mrn {
 
 namespace {
 
+template <int BN, class Epi>
+using ShapeOf = GemmShape<BN, Epi::kWarps, Epi::kOutBytes>;
+
 template <int BN, bool FP8, class Epi>
 cudaError_t launch_one(const GemmPlan& p, const Epi& epi, cudaStream_t stream) {
-  gemm_tc_kernel<BN, FP8, Epi><<<p.grid, kGemmThreads, GemmShape<BN>::kSmemBytes, stream>>>(
+  gemm_tc_kernel<BN, FP8, Epi><<<p.grid, ShapeOf<BN, Epi>::kThreads, ShapeOf<BN, Epi>::kSmemBytes, stream>>>(
       p.map_a, p.map_b, p.map_out, epi, p.args.m, p.args.n, p.args.k, p.args.status);
   return cudaGetLastError();
 }
@@ -48,7 +51,7 @@ cudaError_t launch_fp8(const GemmPlan& p, cudaStream_t stream) {
 template <int BN, bool FP8, class Epi>
 cudaError_t prepare_one() {
   return cudaFuncSetAttribute(gemm_tc_kernel<BN, FP8, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              GemmShape<BN>::kSmemBytes);
+                              ShapeOf<BN, Epi>::kSmemBytes);
 }
 
 template <int BN>
@@ -123,12 +126,6 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
   }
   const int tiles = ((args.m + kTileM - 1) / kTileM) * (args.n / plan->bn);
   plan->grid = tiles < num_sms ? tiles : num_sms;
-  switch (plan->bn) {
-    case 256: plan->smem = GemmShape<256>::kSmemBytes; break;
-    case 192: plan->smem = GemmShape<192>::kSmemBytes; break;
-    case 128: plan->smem = GemmShape<128>::kSmemBytes; break;
-    default: plan->smem = GemmShape<64>::kSmemBytes; break;
-  }
   return true;
 }
 

@@ -6,15 +6,15 @@
 // walks the output tiles (128 rows x BN columns) in n-fastest order, so the CTAs working on
 // the same 128-row block of A at the same time share it through L2.
 //
-// Roles (320 threads):
+// Roles (64 + 32 x epilogue warps threads):
 //   warp 0, one lane : TMA producer. A 128x128-byte tile and a BNx128-byte tile per stage,
 //                      128-byte swizzled, into a STAGES-deep ring of shared-memory buffers.
 //   warp 1, one lane : MMA issuer. 4 tcgen05.mma (K = 32 bytes each) per stage into a TMEM
 //                      accumulator; two accumulators of BN columns alternate between tiles
 //                      so the epilogue of one tile overlaps the MMAs of the next.
-//   warps 2..9       : epilogue. Warp w reads TMEM lanes 32*(w%4).. (one output row per
-//                      thread) in one half of the tile's columns, 32 at a time, applies the
-//                      epilogue functor, writes the
+//   warps 2..        : epilogue (8 warps, 16 for the GELU epilogue). Warp w reads TMEM lanes
+//                      32*(w%4).. (one output row per thread) in its share of the tile's
+//                      columns, 32 at a time, applies the epilogue functor, writes the
 //                      32x32 block into a swizzled shared-memory staging buffer and one lane
 //                      issues a TMA tile store (or, for the residual stream, a TMA reduce-add),
 //                      so global writes are whole swizzle rows issued by the copy engine.
@@ -25,33 +25,35 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_fp8.h>
 
 #include "ptx.cuh"
 
 namespace mrn {
 
-constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, each taking half of the columns
-constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 constexpr int kTileM = 128;
 constexpr int kStageRowBytes = 128;  // one swizzle row: 64 bf16 or 128 e4m3 values of K
 constexpr uint32_t kTmemCols = 512;  // two accumulators of up to 256 f32 columns
-constexpr int kEpiChunk = 32;                       // columns per epilogue step
-constexpr int kEpiBufBytes = 32 * kEpiChunk * 4;    // one 32x32 staging block at up to 4 B
-constexpr int kEpiBytes = kEpiWarps * kEpiBufBytes;  // one staging block per epilogue warp
-constexpr int kMaxSmem = 232448;                    // 227 KB per CTA
+constexpr int kEpiChunk = 32;        // columns per epilogue step
+constexpr int kMaxSmem = 232448;     // 227 KB per CTA
 
-template <int BN>
+// Shared memory of one (BN, epilogue) instantiation: the operand ring plus one 32 x 32 staging
+// block per epilogue warp.
+template <int BN, int EPI_WARPS, int OUT_BYTES>
 struct GemmShape {
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
   static constexpr int kABytes = kTileM * kStageRowBytes;
   static constexpr int kBBytes = BN * kStageRowBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kEpiBufBytes = 32 * kEpiChunk * OUT_BYTES;
+  static constexpr int kEpiBytes = EPI_WARPS * kEpiBufBytes;
   static constexpr int kBarrierBytes = 256;
   static constexpr int kFit = (kMaxSmem - 1024 - kBarrierBytes - kEpiBytes) / kStageBytes;
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
   static_assert(kStages >= 2, "not enough shared memory for a 2-stage pipeline");
   static constexpr int kSmemBytes = 1024 /*alignment slack*/ + kStages * kStageBytes + kEpiBytes + kBarrierBytes;
+  static constexpr int kThreads = 64 + 32 * EPI_WARPS;
 };
 
 __device__ __forceinline__ float rcp_approx(float x) {
@@ -63,23 +65,56 @@ __device__ __forceinline__ float rcp_approx(float x) {
 // GELU(x) = x * Phi(x), Phi(x) = 0.5 (1 + erf(x / sqrt 2)), with erf from Abramowitz & Stegun
 // 7.1.28: erf(z) = 1 - (1 + a1 z + ... + a6 z^6)^-16 for z >= 0, |error| <= 3e-7. One
 // hardware reciprocal and a dozen FMA-pipe operations per element (the epilogue of FFN1
-// evaluates it for every one of the R x d_ff hidden activations). z is clamped at 10, where
-// erf is 1 in f32 and the 16th power stays finite.
+// evaluates it for every one of the R x d_ff hidden activations). The coefficients below are
+// a_k * 2^(1/16), so the 16th power carries the factor 2 and its reciprocal is directly
+// 0.5 (1 - erf(z)), the upper tail of Phi at |x|. z is clamped at 10, where erf is 1 in f32
+// and the 16th power stays finite.
+constexpr float kTwoPow16th = 1.0442737824274138f;  // 2^(1/16)
+constexpr float kErfC0 = 1.0f * kTwoPow16th;
+constexpr float kErfC1 = 0.0705230784f * kTwoPow16th;
+constexpr float kErfC2 = 0.0422820123f * kTwoPow16th;
+constexpr float kErfC3 = 0.0092705272f * kTwoPow16th;
+constexpr float kErfC4 = 0.0001520143f * kTwoPow16th;
+constexpr float kErfC5 = 0.0002765672f * kTwoPow16th;
+constexpr float kErfC6 = 0.0000430638f * kTwoPow16th;
+
 __device__ __forceinline__ float gelu_erf(float x) {
   const float z = fminf(fabsf(x) * 0.70710678118654752f, 10.f);
-  float p = fmaf(z, 4.30638e-5f, 2.765672e-4f);
-  p = fmaf(z, p, 1.520143e-4f);
-  p = fmaf(z, p, 9.2705272e-3f);
-  p = fmaf(z, p, 4.22820123e-2f);
-  p = fmaf(z, p, 7.05230784e-2f);
-  p = fmaf(z, p, 1.f);
+  float p = fmaf(z, kErfC6, kErfC5);
+  p = fmaf(z, p, kErfC4);
+  p = fmaf(z, p, kErfC3);
+  p = fmaf(z, p, kErfC2);
+  p = fmaf(z, p, kErfC1);
+  p = fmaf(z, p, kErfC0);
   p = p * p;  // ^2
   p = p * p;  // ^4
   p = p * p;  // ^8
-  p = p * p;  // ^16
-  const float q = 0.5f * rcp_approx(p);  // 0.5 * (1 - erf(z)) = upper tail of Phi at |x|
-  const float phi = x >= 0.f ? 1.f - q : q;
-  return x * phi;
+  p = p * p;  // ^16 (times 2)
+  const float q = rcp_approx(p);
+  return x * (x >= 0.f ? 1.f - q : q);
+}
+
+// The same on two values in packed f16 arithmetic, for outputs that are rounded to e4m3
+// (3 mantissa bits) right after: f16 keeps the result well inside one e4m3 step, at about half
+// the instructions. Where the 16th power overflows f16 (|x| > ~4.2, erf(z) > 1 - 2e-5) the
+// reciprocal is 0 and Phi is 0 or 1.
+__device__ __forceinline__ __half2 gelu_erf_h2(__half2 x) {
+  const __half2 z = __hmul2(__habs2(x), __float2half2_rn(0.70710678118654752f));
+  __half2 p = __hfma2(z, __float2half2_rn(kErfC6), __float2half2_rn(kErfC5));
+  p = __hfma2(z, p, __float2half2_rn(kErfC4));
+  p = __hfma2(z, p, __float2half2_rn(kErfC3));
+  p = __hfma2(z, p, __float2half2_rn(kErfC2));
+  p = __hfma2(z, p, __float2half2_rn(kErfC1));
+  p = __hfma2(z, p, __float2half2_rn(kErfC0));
+  p = __hmul2(p, p);
+  p = __hmul2(p, p);
+  p = __hmul2(p, p);
+  p = __hmul2(p, p);
+  const __half2 q = h2rcp(p);
+  // Phi = q + [x >= 0] (1 - 2q)
+  const __half2 ge = __hge2(x, __float2half2_rn(0.f));
+  const __half2 phi = __hfma2(ge, __hfma2(q, __float2half2_rn(-2.f), __float2half2_rn(1.f)), q);
+  return __hmul2(x, phi);
 }
 
 // Byte offset of 16-byte chunk `j` of row `r` in a staging block whose rows are RB bytes and
@@ -100,6 +135,7 @@ __device__ __forceinline__ int staged_offset(int r, int j) {
 struct EpiBiasBf16 {
   static constexpr int kOutBytes = 2;
   static constexpr bool kReduce = false;
+  static constexpr int kWarps = 8;
   const float* bias;
   float scale;
   __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[4]) const {
@@ -118,39 +154,43 @@ struct EpiBiasBf16 {
 };
 
 // out = GELU(acc * scale + bias) as bf16, or as e4m3 codes of value * inv_q (saturating).
+// The GELU is the bulk of the epilogue's arithmetic, so it gets 16 warps.
 template <bool E4M3>
 struct EpiGelu {
   static constexpr int kOutBytes = E4M3 ? 1 : 2;
   static constexpr bool kReduce = false;
+  static constexpr int kWarps = 16;
   const float* bias;
   float scale;
   float inv_q;
   __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[kOutBytes * 2]) const {
-    float g[32];
-#pragma unroll
-    for (int c = 0; c < 32; c += 4) {
-      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c));
-      g[c + 0] = gelu_erf(v[c + 0] * scale + b.x);
-      g[c + 1] = gelu_erf(v[c + 1] * scale + b.y);
-      g[c + 2] = gelu_erf(v[c + 2] * scale + b.z);
-      g[c + 3] = gelu_erf(v[c + 3] * scale + b.w);
-    }
     if constexpr (E4M3) {
+      const __half2 iq = __float2half2_rn(inv_q);
 #pragma unroll
       for (int c = 0; c < 32; c += 16) {
         __nv_fp8x2_storage_t q[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          q[j] = __nv_cvt_float2_to_fp8x2(make_float2(g[c + 2 * j] * inv_q, g[c + 2 * j + 1] * inv_q), __NV_SATFINITE,
-                                          __NV_E4M3);
+        for (int j = 0; j < 8; j += 2) {
+          const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c + 2 * j));
+          const __half2 x0 = __floats2half2_rn(v[c + 2 * j] * scale + b.x, v[c + 2 * j + 1] * scale + b.y);
+          const __half2 x1 = __floats2half2_rn(v[c + 2 * j + 2] * scale + b.z, v[c + 2 * j + 3] * scale + b.w);
+          const __half2 y0 = __hmul2(gelu_erf_h2(x0), iq);
+          const __half2 y1 = __hmul2(gelu_erf_h2(x1), iq);
+          q[j] = __nv_cvt_halfraw2_to_fp8x2(y0, __NV_SATFINITE, __NV_E4M3);
+          q[j + 1] = __nv_cvt_halfraw2_to_fp8x2(y1, __NV_SATFINITE, __NV_E4M3);
+        }
         o[c / 16] = *reinterpret_cast<const uint4*>(q);
       }
     } else {
 #pragma unroll
       for (int c = 0; c < 32; c += 8) {
+        const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + col + c));
+        const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + col + c + 4));
         __nv_bfloat162 p[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) p[j] = __floats2bfloat162_rn(g[c + 2 * j], g[c + 2 * j + 1]);
+        p[0] = __floats2bfloat162_rn(gelu_erf(v[c + 0] * scale + b0.x), gelu_erf(v[c + 1] * scale + b0.y));
+        p[1] = __floats2bfloat162_rn(gelu_erf(v[c + 2] * scale + b0.z), gelu_erf(v[c + 3] * scale + b0.w));
+        p[2] = __floats2bfloat162_rn(gelu_erf(v[c + 4] * scale + b1.x), gelu_erf(v[c + 5] * scale + b1.y));
+        p[3] = __floats2bfloat162_rn(gelu_erf(v[c + 6] * scale + b1.z), gelu_erf(v[c + 7] * scale + b1.w));
         o[c / 8] = *reinterpret_cast<const uint4*>(p);
       }
     }
@@ -161,6 +201,7 @@ struct EpiGelu {
 struct EpiResidual {
   static constexpr int kOutBytes = 4;
   static constexpr bool kReduce = true;
+  static constexpr int kWarps = 8;
   const float* bias;
   float scale;
   __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[8]) const {
@@ -176,11 +217,14 @@ struct EpiResidual {
 
 // ---- the kernel ------------------------------------------------------------------------
 template <int BN, bool FP8, class Epi>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_out, Epi epi, int M, int N, int K, int* status) {
-  using S = GemmShape<BN>;
+  using S = GemmShape<BN, Epi::kWarps, Epi::kOutBytes>;
   constexpr int kStages = S::kStages;
+  constexpr int kEpiWarps = Epi::kWarps;
+  constexpr int kEpiBufBytes = S::kEpiBufBytes;
+  constexpr int kEpiBytes = S::kEpiBytes;
   constexpr int kElemsPerStage = FP8 ? 128 : 64;
   constexpr uint32_t kIdesc = FP8 ? idesc_e4m3(kTileM, BN) : idesc_bf16(kTileM, BN);
   constexpr int kRowBytes = kEpiChunk * Epi::kOutBytes;  // staged bytes per output row
@@ -316,11 +360,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ---- epilogue: warps 2..9; warp w reads TMEM lane quarter w % 4 and one half of the
-    // tile's columns
+    // ---- epilogue: warps 2..; warp w reads TMEM lane quarter w % 4 and takes every
+    // kParts-th 32-column chunk of the tile, starting at its part index.
+    constexpr int kParts = kEpiWarps / 4;
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
-    constexpr int kHalf = BN / 2;
+    const int part = (warp - 2) >> 2;
     uint8_t* sb = sm_epi + (warp - 2) * kEpiBufBytes;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -335,10 +379,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int row0 = m0 + quarter * 32;
 #pragma unroll 1
-      for (int c = half * kHalf; c < (half + 1) * kHalf; c += kEpiChunk) {
+      for (int c = part * kEpiChunk; c < BN; c += kParts * kEpiChunk) {
         float v[32];
         tmem_ld32(taddr + c, v);
-        if (c + kEpiChunk >= (half + 1) * kHalf) {
+        if (c + kParts * kEpiChunk >= BN) {
           // Last TMEM read of this tile by this warp: hand the accumulator back.
           tc_fence_before();
           __syncwarp();
@@ -363,6 +407,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           bulk_commit();
         }
+      }
+      if (part * kEpiChunk >= BN) {
+        // A warp without a chunk in this tile still releases the accumulator.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tmem_empty[acc]);
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;

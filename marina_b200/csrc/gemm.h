@@ -36,7 +36,6 @@ struct GemmPlan {
   GemmArgs args;
   int bn = 0;
   int grid = 0;
-  int smem = 0;
 };
 
 // Widest supported N tile (256, 192, 128, 64) dividing n; 0 if none.
