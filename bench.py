@@ -48,6 +48,13 @@ def parse_args():
     ap.add_argument("--precision", choices=["fp8", "fp8w", "bf16"], default="fp8")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", choices=["step", "sweep", "puct", "wholebox"], default="step",
+                    help="step: the contract's JSON line; sweep: configs[2] latency/throughput per batch size; "
+                         "puct: configs[3] nodes/s of the batched PUCT search; wholebox: configs[4] 1M positions")
+    ap.add_argument("--roots", type=int, default=32)
+    ap.add_argument("--nodes", type=int, default=100_000)
+    ap.add_argument("--positions", type=int, default=1 << 20)
+    ap.add_argument("--chunk", type=int, default=8192)
     return ap.parse_args()
 
 
@@ -328,10 +335,140 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ---- batch sweep on one GPU ----------------------------------------------------
+def run_sweep(args):
+    import torch
+
+    from marina_b200 import chess
+    from marina_b200.network import B200Network
+
+    arch, w = load_net(args.net)
+    sizes = [1, 16, 64, 256, 1024, 4096, 8192]
+    net = B200Network(arch, w, device=0, max_batch=max(sizes), precision=args.precision)
+    boards, legal, _, _ = chess.random_positions(1, max(sizes), 0, 80)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    d_boards, d_legal = torch.from_numpy(boards).to(dev), torch.from_numpy(legal).to(dev)
+    d_priors, d_wdl = torch.empty((max(sizes), 224), device=dev), torch.empty((max(sizes), 3), device=dev)
+    for b in sizes:
+        step = lambda: net.evaluate_device(b, d_boards.data_ptr(), d_legal.data_ptr(), d_priors.data_ptr(),  # noqa: E731
+                                           d_wdl.data_ptr(), stream.cuda_stream)
+        for _ in range(args.warmup):
+            step()
+        times = []
+        for _ in range(args.steps):
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            step()
+            s1.record(stream)
+            s1.synchronize()
+            times.append(s0.elapsed_time(s1))
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            net.evaluate_packed(boards[:b], legal[:b])
+        e2e_ms = (time.perf_counter() - t0) / args.steps * 1e3
+        prof = net.profile(b, d_boards.data_ptr(), d_legal.data_ptr(), d_priors.data_ptr(), d_wdl.data_ptr(),
+                           stream.cuda_stream)
+        g = prof["gemm"]
+        p50 = float(np.median(times))
+        print(json.dumps({"mode": "sweep", "net": args.net, "precision": args.precision, "batch": b,
+                          "latency_ms_p50": p50, "evals_per_s": b / (p50 / 1e3), "e2e_latency_ms": e2e_ms,
+                          "e2e_evals_per_s": b / (e2e_ms / 1e3), "gemm_tflops": g["flops"] / (g["ms"] / 1e3) / 1e12,
+                          "kernel_ms": {k: round(v["ms"], 4) for k, v in prof.items()}}), flush=True)
+    net.close()
+
+
+# ---- batched PUCT nodes/s on N GPUs (one process, per-GPU evaluator threads) -----
+def run_puct(args):
+    import ctypes
+
+    from marina_b200 import _lib, chess, search
+    from marina_b200.network import B200Network
+
+    arch, w = load_net(args.net)
+    n_gpus = args.gpus
+    workers = 2  # two gathering threads per GPU: one gathers while the other's batch is evaluated
+    roots_per_worker = -(-args.roots // (n_gpus * workers))
+    nets = [B200Network(arch, w, device=g, max_batch=roots_per_worker * 256, precision=args.precision)
+            for g in range(n_gpus)]
+    _, _, _, fens = chess.random_positions(1, args.roots, 0, 80, fens=True)
+    roots = [chess.from_fen(f) for f in fens]
+    fn = ctypes.cast(_lib.load().mrn_evaluate, ctypes.c_void_p).value
+    evaluators = [(fn, net._ctx.value) for net in nets]
+    warm, _ = search.search(roots[:max(1, n_gpus)], 2000, evaluators, workers)  # graphs, clocks
+    per_root, total = search.search(roots, args.nodes, evaluators, workers, search.default_params(256))
+    print(json.dumps({"mode": "puct", "net": args.net, "precision": args.precision, "gpus": n_gpus,
+                      "roots": args.roots, "node_limit": args.nodes, "leaf_batch": 256,
+                      "nodes": total["nodes"], "seconds": total["seconds"],
+                      "nodes_per_s": total["nodes"] / total["seconds"],
+                      "network_evals": total["network_evals"], "collisions": total["collisions"],
+                      "max_depth": total["max_depth"], "workers_per_gpu": workers,
+                      "describe": nets[0].describe()}), flush=True)
+    for net in nets:
+        net.close()
+
+
+# ---- whole-box throughput, 1M positions in 8192-position chunks over N GPUs -----
+def run_wholebox(args):
+    from concurrent.futures import ThreadPoolExecutor
+
+    import torch
+
+    from marina_b200 import chess
+    from marina_b200.network import B200Network
+
+    arch, w = load_net(args.net)
+    n_gpus, chunk = args.gpus, args.chunk
+    t0 = time.perf_counter()
+    boards, legal, _, _ = chess.random_positions(1, args.positions, 0, 80)
+    gen_s = time.perf_counter() - t0
+    nets = [B200Network(arch, w, device=g, max_batch=chunk, precision=args.precision) for g in range(n_gpus)]
+    chunks = [(a, min(a + chunk, args.positions)) for a in range(0, args.positions, chunk)]
+
+    def shard(g):
+        # pinned staging per GPU: the host->device copies run at full PCIe speed
+        hb = torch.empty((chunk, 66), dtype=torch.uint8).pin_memory().numpy()
+        hl = torch.empty((chunk, 224), dtype=torch.int32).pin_memory().numpy()
+        hp = torch.empty((chunk, 224)).pin_memory().numpy()
+        hw = torch.empty((chunk, 3)).pin_memory().numpy()
+        nets[g].evaluate_packed(boards[:chunk], legal[:chunk], hp, hw)  # warm the bucket's graph
+        return hb, hl, hp, hw
+
+    with ThreadPoolExecutor(n_gpus) as pool:
+        bufs = list(pool.map(shard, range(n_gpus)))
+
+        def work(g):
+            hb, hl, hp, hw = bufs[g]
+            checksum = 0.0
+            for a, b in chunks[g::n_gpus]:
+                n = b - a
+                hb[:n], hl[:n] = boards[a:b], legal[a:b]
+                nets[g].evaluate_packed(hb[:n], hl[:n], hp[:n], hw[:n])
+                checksum += float(hw[:n, 0].sum())
+            return checksum
+
+        t0 = time.perf_counter()
+        sums = list(pool.map(work, range(n_gpus)))
+        el = time.perf_counter() - t0
+    print(json.dumps({"mode": "wholebox", "net": args.net, "precision": args.precision, "gpus": n_gpus,
+                      "positions": args.positions, "chunk": chunk, "seconds": el, "evals_per_s": args.positions / el,
+                      "path": "mrn_evaluate per chunk (host pinned buffers, H2D + graph + D2H), one thread per GPU",
+                      "input_generation_s": gen_s, "wdl_win_sum": sum(sums)}), flush=True)
+    for net in nets:
+        net.close()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.mode == "sweep":
+        run_sweep(args)
+    elif args.mode == "puct":
+        run_puct(args)
+    elif args.mode == "wholebox":
+        run_wholebox(args)
     else:
         run_ours(args)
 

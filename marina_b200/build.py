@@ -4,7 +4,9 @@ files travel with the source tree:
 * ``libmarina_b200.so`` -- the CUDA evaluator (sm_100a only) and its C ABI
   (``include/marina_b200.h``);
 * ``libmarina_chess.so`` -- the host-side position library (move generation, the
-  reference's board/action encoding, seeded random playouts; ``include/marina_chess.h``).
+  reference's board/action encoding, seeded random playouts; ``include/marina_chess.h``) and
+  the batched PUCT search that drives the evaluator for the nodes/s measurement
+  (``include/marina_search.h``).
 
 ``python -m marina_b200.build`` builds both. Rebuilds are skipped when the output is newer
 than every source.
@@ -27,7 +29,7 @@ CHESS_LIB = PKG / "libmarina_chess.so"
 
 CUDA_SOURCES = ["gemm.cu", "kernels.cu", "runtime.cu", "api_test.cu"]
 CUDA_HEADERS = ["ptx.cuh", "gemm.cuh", "gemm.h", "tmap.h", "kernels.cuh", "runtime.h"]
-CHESS_SOURCES = ["chess.cpp"]
+CHESS_SOURCES = ["chess.cpp", "puct.cpp"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -82,11 +84,11 @@ def build_cuda(force: bool = False, verbose: bool = False) -> Path:
 
 def build_chess(force: bool = False) -> Path:
     srcs = [CSRC / s for s in CHESS_SOURCES]
-    deps = srcs + [CSRC / "chess.h", INCLUDE / "marina_chess.h", Path(__file__)]
+    deps = srcs + [INCLUDE / "marina_chess.h", INCLUDE / "marina_search.h", Path(__file__)]
     if not force and not _stale(CHESS_LIB, deps):
         return CHESS_LIB
     tmp = CHESS_LIB.with_suffix(".so.tmp")
-    _run(["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", "-pthread", f"-I{INCLUDE}",
+    _run(["g++", "-O3", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", "-pthread", f"-I{INCLUDE}",
           *map(str, srcs), "-o", str(tmp)])
     tmp.replace(CHESS_LIB)
     return CHESS_LIB

@@ -1,0 +1,61 @@
+"""The batched PUCT harness on the CPU with a fake network (uniform priors, value from the
+board), checking the search bookkeeping the reference's tests check
+(src/search/mod.rs:1560, :1631-1647): node limits are met, every virtual visit is released,
+collisions are counted, and the chosen move is legal."""
+
+import ctypes
+
+import numpy as np
+
+from marina_b200 import chess, search
+
+calls = []
+
+
+@search.EVAL_FN
+def uniform_net(ctx, n, boards, legal, priors, wdl):
+    calls.append(n)
+    lg = np.ctypeslib.as_array(legal, shape=(n, 224))
+    pr = np.ctypeslib.as_array(priors, shape=(n, 224))
+    wd = np.ctypeslib.as_array(wdl, shape=(n, 3))
+    counts = (lg >= 0).sum(1, keepdims=True)
+    pr[:] = np.where(lg >= 0, 1.0 / np.maximum(counts, 1), 0.0)
+    bd = np.ctypeslib.as_array(boards, shape=(n, 66)).astype(np.float32)
+    wd[:, 0] = 0.3 + 0.01 * (bd[:, :64] > 6).sum(1) / 16
+    wd[:, 1] = 0.4
+    wd[:, 2] = 1 - wd[:, 0] - wd[:, 1]
+    return 0
+
+
+def test_search_meets_node_limits_and_picks_legal_moves():
+    roots = [chess.startpos(), chess.from_fen("r3k2r/p1ppqpb1/bn2pnp1/3PN3/1p2P3/2N2Q1p/PPPBBPPP/R3K2R w KQkq - 0 1"),
+             chess.from_fen("8/1P2k3/8/8/8/8/4K1p1/8 w - - 0 1")]
+    calls.clear()
+    per_root, total = search.search(roots, 3000, [(uniform_net, None)], workers_per_evaluator=2,
+                                    params=search.default_params(64))
+    assert total["error"] == 0
+    for root, s in zip(roots, per_root):
+        assert 3000 <= s["nodes"] < 3000 + 64
+        assert s["network_evals"] <= s["nodes"]
+        assert s["best_action"] in chess.legal_actions(root).tolist()
+        assert s["tree_nodes"] > s["network_evals"]
+    assert total["nodes"] == sum(s["nodes"] for s in per_root)
+    assert max(calls) <= 2 * 64  # each worker sends at most its roots' batches in one call
+    assert total["collisions"] > 0
+
+
+def test_mate_in_one_root_is_found_without_the_network_deciding():
+    # White mates with Ra8#: a terminal child backs up -1 for Black, i.e. +1 for White.
+    root = chess.from_fen("6k1/5ppp/8/8/8/8/8/R5K1 w - - 0 1")
+    per_root, _ = search.search([root], 2000, [(uniform_net, None)], workers_per_evaluator=1,
+                                params=search.default_params(32))
+    mate = chess.encode_move(root, chess.parse_uci(root, "a1a8"))
+    assert per_root[0]["best_action"] == mate
+
+
+def test_terminal_root_uses_no_network_slot():
+    calls.clear()
+    stalemate = chess.from_fen("7k/5Q2/6K1/8/8/8/8/8 b - - 0 1")
+    per_root, _ = search.search([stalemate], 100, [(uniform_net, None)], workers_per_evaluator=1,
+                                params=search.default_params(16))
+    assert per_root[0]["network_evals"] == 0 and per_root[0]["nodes"] >= 100 and not calls
