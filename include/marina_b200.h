@@ -185,6 +185,20 @@ MRN_API const char* mrn_last_error(mrn_ctx* ctx);
 
 MRN_API void mrn_destroy(mrn_ctx* ctx);
 
+/* The forward pass of `mrn_evaluate_device` for callers that cannot allocate device memory
+ * once running (a host whose device memory belongs to another allocator, a thread that must
+ * not stall on an allocation, a device that is already full). It allocates nothing: all
+ * intermediate buffers live in one 8 MiB array compiled into the library, resident on every
+ * GPU that loads it for the life of the process. Batches are limited to what fits that array
+ * (11 positions for the `small` network in bf16/fp8w, 15 in fp8; 30 / 41 for `nano`); larger
+ * ones return MRN_ERR_BATCH_TOO_LARGE. Inputs and outputs are the caller's device buffers, as
+ * for `mrn_evaluate_device`. Every call on a device shares the array, so calls whose GPU work
+ * overlaps (other streams, other contexts on the same device) corrupt each other's results:
+ * serialise them. The first call on a device looks the array's address up; make it before any
+ * stream capture. This entry point has no counterpart in the reference. */
+MRN_API int mrn_evaluate_device_static(mrn_ctx* ctx, int n, const uint8_t* d_boards, const int32_t* d_legal,
+                                       float* d_priors, float* d_wdl, void* stream);
+
 /* ---- kernel-level entry points for the GPU test-suite (device pointers, caller's stream) */
 
 /* One GEMM launch: out = epilogue(a[m,k] . b[n,k]^T * scale + bias). `fp8` selects e4m3

@@ -30,7 +30,7 @@ PROFILE_SLOTS = ("embed", "layernorm", "gemm", "attention", "heads")
 EXPORTS = (
     "mrn_create", "mrn_evaluate", "mrn_logits", "mrn_evaluate_device", "mrn_status_word",
     "mrn_profile", "mrn_launches_per_forward", "mrn_describe", "mrn_last_error", "mrn_destroy",
-    "mrn_test_gemm", "mrn_test_last_error",
+    "mrn_test_gemm", "mrn_test_last_error", "mrn_evaluate_device_static",
 )
 
 
@@ -77,6 +77,7 @@ def load() -> ctypes.CDLL:
         "mrn_evaluate": (c_int, [c_void_p, c_int, POINTER(c_uint8), POINTER(c_int32), POINTER(c_float), POINTER(c_float)]),
         "mrn_logits": (c_int, [c_void_p, c_int, POINTER(c_uint8), POINTER(c_float), POINTER(c_float)]),
         "mrn_evaluate_device": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+        "mrn_evaluate_device_static": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
         "mrn_status_word": (c_int, [c_void_p, POINTER(c_int)]),
         "mrn_profile": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                 POINTER(c_float), POINTER(c_double), POINTER(c_int)]),

@@ -1,0 +1,192 @@
+// A forward pass that allocates no device memory: every intermediate buffer of the pass lives in
+// one statically sized device array compiled into the library.
+//
+// Who needs it: callers that must not call cudaMalloc once they are running -- a host process
+// whose device memory belongs to another allocator (a framework's caching pool, a plugin host
+// that fixes its footprint at start-up), a latency-critical thread where an allocation can stall
+// on a device-wide synchronisation, or code that must keep working when the device is full.
+// They can still evaluate small batches (the search's root, a handful of leaves) through
+// `mrn_evaluate_device_static`, with the weights already loaded by `mrn_create`.
+//
+// The array holds kStaticScratchBytes (8 MiB) and is resident on every GPU that loads this
+// library, for the life of the process. How many positions fit depends on the network: one
+// position needs 65 rows of the residual stream (f32), the two GEMM inputs and the attention
+// output (bf16, or e4m3 for MRN_PRECISION_FP8), Q/K/V (bf16) and the FFN hidden layer, plus
+// two d-wide bf16 rows for the value head -- 0.73 MB for the `small` network in bf16 or fp8w
+// (11 positions; 15 in fp8) and 0.28 MB for `nano` (30 positions; 41 in fp8). Larger batches
+// are refused with MRN_ERR_BATCH_TOO_LARGE and a message naming the limit.
+//
+// The first call on a device looks up the array's device address (cudaGetSymbolAddress, once
+// per device, with that device current); make that first call before capturing a stream.
+//
+// All calls on a device share the array. Nothing in it has to start at zero (every buffer is
+// written before it is read), so nothing is cleared, but two calls whose GPU work overlaps --
+// on different streams, or through different contexts on the same device -- overwrite each
+// other's intermediates: serialise them. Device-side errors go to the context's status word
+// (`mrn_status_word`).
+#include <cuda_bf16.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "../../include/marina_b200.h"
+#include "gemm.h"
+#include "kernels.cuh"
+#include "runtime.h"
+
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
+
+// Byte offsets of the pass's buffers for `n` positions inside the array.
+struct Layout {
+  size_t x, h, qkv, attn, ff, vnorm, vhid, end;
+};
+
+Layout layout(const mrn_ctx* c, int n) {
+  const size_t R = static_cast<size_t>(n) * c->t, d = c->d, ab = c->act_bytes;
+  Layout l;
+  l.x = 0;
+  l.h = l.x + align256(R * d * 4);
+  l.qkv = l.h + align256(R * d * ab);
+  l.attn = l.qkv + align256(R * 3 * d * 2);
+  l.ff = l.attn + align256(R * d * ab);
+  l.vnorm = l.ff + align256(R * c->dff * ab);
+  l.vhid = l.vnorm + align256(static_cast<size_t>(n) * d * 2);
+  l.end = l.vhid + align256(static_cast<size_t>(n) * d * 2);
+  return l;
+}
+
+int max_positions(const mrn_ctx* c) {
+  int n = 0;
+  while (layout(c, n + 1).end <= kStaticScratchBytes) ++n;
+  return n;
+}
+
+// The device address of the array on the current device, looked up once per device: in host
+// code `g_static_scratch` names a host-side stand-in, not device memory.
+int scratch_address(mrn_ctx* c, uint8_t** out) {
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (c->device < 0 || c->device >= kMaxDevices) return c->fail(MRN_ERR_UNSUPPORTED, "device %d", c->device);
+  if (!g_scratch_addr[c->device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess || !p)
+      return c->fail(MRN_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
+    g_scratch_addr[c->device] = p;
+  }
+  *out = static_cast<uint8_t*>(g_scratch_addr[c->device]);
+  return MRN_OK;
+}
+
+#define CKS(call)                                                                                    \
+  do {                                                                                               \
+    const cudaError_t e_ = (call);                                                                   \
+    if (e_ != cudaSuccess) return c->fail(MRN_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_));   \
+  } while (0)
+
+// Plan one GEMM on the stack and launch it.
+int gemm(mrn_ctx* c, const mrn::GemmArgs& a, cudaStream_t s) {
+  mrn::GemmPlan p;
+  char err[256];
+  if (!mrn::gemm_plan(&p, a, c->num_sms, err)) return c->fail(MRN_ERR_UNSUPPORTED, "%s", err);
+  CKS(mrn::gemm_launch(p, s));
+  return MRN_OK;
+}
+
+// The forward pass of the graph path (embed, layers, heads), with the array's buffers and the
+// caller's inputs and outputs.
+int forward(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, float* priors, float* wdl, uint8_t* base,
+            cudaStream_t s) {
+  using mrn::ActType;
+  using mrn::Epilogue;
+  const Layout L = layout(c, n);
+  float* x = reinterpret_cast<float*>(base + L.x);
+  void* h = base + L.h;
+  __nv_bfloat16* qkv = reinterpret_cast<__nv_bfloat16*>(base + L.qkv);
+  void* attn = base + L.attn;
+  void* ff = base + L.ff;
+  __nv_bfloat16* vnorm = reinterpret_cast<__nv_bfloat16*>(base + L.vnorm);
+  __nv_bfloat16* vhid = reinterpret_cast<__nv_bfloat16*>(base + L.vhid);
+  const int R = n * c->t, d = c->d, ff_dim = c->dff;
+  const ActType act = c->act;
+  const bool fp8 = c->precision == MRN_PRECISION_FP8;
+  int rc;
+
+  const mrn::DevLayer& D0 = c->dl[0];
+  CKS(mrn::launch_embed_ln(
+      mrn::EmbedParams{boards, c->piece, c->square, c->state, c->cast_w, c->cast_b, c->ep, x, c->t, c->square_start},
+      mrn::NormParams{D0.n1g, D0.n1b, c->eps, h, act, 1.f / D0.as[0]}, n, d, s));
+  for (int l = 0; l < c->layers; ++l) {
+    const mrn::DevLayer& D = c->dl[l];
+    auto scale = [&](int i) { return fp8 ? D.ws[i] * D.as[i] : D.ws[i]; };
+    mrn::GemmArgs g;
+    g.m = R, g.fp8 = fp8, g.status = c->status;
+    mrn::GemmArgs q = g;
+    q.a = h, q.b = D.w_qkv, q.n = 3 * d, q.k = d, q.epi = Epilogue::kBias, q.out = qkv, q.ldo = 3 * d;
+    q.bias = D.b_qkv, q.scale = scale(0);
+    if ((rc = gemm(c, q, s))) return rc;
+    CKS(mrn::launch_attention(mrn::AttentionParams{qkv, attn, act, 1.f / D.as[1], c->t, d, c->heads}, n,
+                              d / c->heads, s));
+    mrn::GemmArgs o = g;
+    o.a = attn, o.b = D.w_o, o.n = d, o.k = d, o.epi = Epilogue::kResidual, o.out = x, o.ldo = d;
+    o.bias = D.b_o, o.scale = scale(1);
+    if ((rc = gemm(c, o, s))) return rc;
+    CKS(mrn::launch_layernorm(x, mrn::NormParams{D.n2g, D.n2b, c->eps, h, act, 1.f / D.as[2]}, R, d, s));
+    mrn::GemmArgs f1 = g;
+    f1.a = h, f1.b = D.w_1, f1.n = ff_dim, f1.k = d, f1.epi = fp8 ? Epilogue::kGeluE4m3 : Epilogue::kGeluBf16;
+    f1.out = ff, f1.ldo = ff_dim, f1.bias = D.b_1, f1.scale = scale(2), f1.inv_q = 1.f / D.as[3];
+    if ((rc = gemm(c, f1, s))) return rc;
+    mrn::GemmArgs f2 = g;
+    f2.a = ff, f2.b = D.w_2, f2.n = d, f2.k = ff_dim, f2.epi = Epilogue::kResidual, f2.out = x, f2.ldo = d;
+    f2.bias = D.b_2, f2.scale = scale(3);
+    if ((rc = gemm(c, f2, s))) return rc;
+    if (l + 1 < c->layers) {
+      const mrn::DevLayer& N = c->dl[l + 1];
+      CKS(mrn::launch_layernorm(x, mrn::NormParams{N.n1g, N.n1b, c->eps, h, act, 1.f / N.as[0]}, R, d, s));
+    }
+  }
+  mrn::HeadsParams hp;
+  hp.x = x, hp.final_g = c->fn_g, hp.final_b = c->fn_b, hp.policy_g = c->pn_g, hp.policy_b = c->pn_b;
+  hp.policy_w = c->pw, hp.policy_bias = c->pb, hp.value_g = c->vn_g, hp.value_b = c->vn_b;
+  hp.legal = legal, hp.slots = MRN_MAX_LEGAL, hp.softmax = 1, hp.priors = priors;
+  hp.value_in = vnorm, hp.status = c->status, hp.eps = c->eps, hp.t = c->t, hp.square_start = c->square_start;
+  CKS(mrn::launch_heads(hp, n, d, s));
+  mrn::GemmArgs v;
+  v.m = n, v.n = d, v.k = d, v.fp8 = false, v.status = c->status;
+  v.a = vnorm, v.b = c->vw1, v.epi = Epilogue::kGeluBf16, v.out = vhid, v.ldo = d, v.bias = c->vb1;
+  if ((rc = gemm(c, v, s))) return rc;
+  CKS(mrn::launch_value_out(mrn::ValueOutParams{vhid, c->vw2, c->vb2, wdl, 1}, n, d, s));
+  return MRN_OK;
+}
+
+}  // namespace
+
+extern "C" MRN_API int mrn_evaluate_device_static(mrn_ctx* c, int n, const uint8_t* d_boards, const int32_t* d_legal,
+                                                  float* d_priors, float* d_wdl, void* stream) {
+  if (!c) return MRN_ERR_ARGUMENT;
+  std::lock_guard<std::mutex> lock(c->mu);
+  if (n < 0) return c->fail(MRN_ERR_ARGUMENT, "n = %d", n);
+  if (n == 0) return MRN_OK;
+  if (!d_boards || !d_legal || !d_priors || !d_wdl) return c->fail(MRN_ERR_ARGUMENT, "NULL buffer");
+  const int limit = max_positions(c);
+  if (n > limit)
+    return c->fail(MRN_ERR_BATCH_TOO_LARGE,
+                   "batch of %d positions exceeds the %d that fit the %zu-byte static scratch for this network", n,
+                   limit, kStaticScratchBytes);
+  const cudaError_t e = cudaSetDevice(c->device);
+  if (e != cudaSuccess) return c->fail(MRN_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+  uint8_t* base = nullptr;
+  const int rc = scratch_address(c, &base);
+  if (rc) return rc;
+  return forward(c, n, d_boards, d_legal, d_priors, d_wdl, base,
+                 stream ? static_cast<cudaStream_t>(stream) : c->stream);
+}

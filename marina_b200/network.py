@@ -194,6 +194,16 @@ class B200Network(Network):
                                            c_void_p(priors_ptr), c_void_p(wdl_ptr), c_void_p(stream or 0))
         self._check(rc, "device forward")
 
+    def evaluate_device_static(self, n: int, boards_ptr: int, legal_ptr: int, priors_ptr: int, wdl_ptr: int,
+                               stream: int | None = None) -> None:
+        """`evaluate_device` without any device allocation: the pass's intermediates live in the
+        library's static 8 MiB device array, so it serves callers that must not allocate once
+        running, for small batches (see `mrn_evaluate_device_static`). Calls whose GPU work
+        overlaps share that array and race; serialise them."""
+        rc = self._lib.mrn_evaluate_device_static(self._ctx, n, c_void_p(boards_ptr), c_void_p(legal_ptr),
+                                                  c_void_p(priors_ptr), c_void_p(wdl_ptr), c_void_p(stream or 0))
+        self._check(rc, "static-scratch forward")
+
     def status_word(self) -> int:
         word = c_int()
         self._check(self._lib.mrn_status_word(self._ctx, ctypes.byref(word)), "status")
