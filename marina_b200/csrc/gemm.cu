@@ -1,5 +1,6 @@
 // Instantiations and host dispatch of the tcgen05 GEMM.
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "gemm.cuh"
 #include "gemm.h"
@@ -17,6 +18,47 @@ cudaError_t launch_one(const GemmPlan& p, const Epi& epi, cudaStream_t stream) {
   gemm_tc_kernel<BN, FP8, Epi><<<p.grid, ShapeOf<BN, Epi>::kThreads, ShapeOf<BN, Epi>::kSmemBytes, stream>>>(
       p.map_a, p.map_b, p.map_out, epi, p.args.m, p.args.n, p.args.k, p.args.status);
   return cudaGetLastError();
+}
+
+template <bool FP8, class Epi>
+cudaError_t launch_pair(const GemmPlan& p, const Epi& epi, cudaStream_t stream) {
+  using P = PairShape<Epi::kOutBytes, Epi::kWarps>;
+  gemm_pair_kernel<FP8, Epi><<<p.grid, P::kThreads, P::kSmemBytes, stream>>>(p.map_a, p.map_b, p.map_out, epi,
+                                                                            p.args.m, p.args.n, p.args.k,
+                                                                            p.args.status);
+  return cudaGetLastError();
+}
+
+template <bool FP8>
+cudaError_t launch_pair_epi(const GemmPlan& p, cudaStream_t stream) {
+  const GemmArgs& a = p.args;
+  switch (a.epi) {
+    case Epilogue::kBias:
+      return launch_pair<FP8>(p, EpiBiasBf16{a.bias, a.scale}, stream);
+    case Epilogue::kResidual:
+      return launch_pair<FP8>(p, EpiResidual{a.bias, a.scale}, stream);
+    case Epilogue::kGeluBf16:
+      if constexpr (!FP8) return launch_pair<FP8>(p, EpiGelu<false>{a.bias, a.scale, a.inv_q}, stream);
+      break;
+    case Epilogue::kGeluE4m3:
+      if constexpr (FP8) return launch_pair<FP8>(p, EpiGelu<true>{a.bias, a.scale, a.inv_q}, stream);
+      break;
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <bool FP8, class Epi>
+cudaError_t prepare_pair() {
+  return cudaFuncSetAttribute(gemm_pair_kernel<FP8, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              PairShape<Epi::kOutBytes, Epi::kWarps>::kSmemBytes);
+}
+
+bool pair_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("MRN_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 template <int BN, bool FP8>
@@ -102,8 +144,9 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
     snprintf(err, 256, "gemm: output/bias misaligned or ldo %d < N %d", args.ldo, args.n);
     return false;
   }
+  plan->pair = pair_enabled() && args.n % 256 == 0;
   if (!make_kmajor_map(&plan->map_a, args.a, eb, args.m, args.k, kTileM) ||
-      !make_kmajor_map(&plan->map_b, args.b, eb, args.n, args.k, plan->bn)) {
+      !make_kmajor_map(&plan->map_b, args.b, eb, args.n, args.k, plan->pair ? 128 : plan->bn)) {
     snprintf(err, 256, "gemm: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", args.m, args.n, args.k);
     return false;
   }
@@ -124,13 +167,25 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
     snprintf(err, 256, "gemm: output tensor map failed (M=%d N=%d ldo=%d)", args.m, args.n, args.ldo);
     return false;
   }
-  const int tiles = ((args.m + kTileM - 1) / kTileM) * (args.n / plan->bn);
-  plan->grid = tiles < num_sms ? tiles : num_sms;
+  if (plan->pair) {
+    const int tiles = ((args.m + 2 * kTileM - 1) / (2 * kTileM)) * (args.n / 256);
+    const int pairs = num_sms / 2;
+    plan->grid = 2 * (tiles < pairs ? tiles : pairs);
+  } else {
+    const int tiles = ((args.m + kTileM - 1) / kTileM) * (args.n / plan->bn);
+    plan->grid = tiles < num_sms ? tiles : num_sms;
+  }
   return true;
 }
 
 cudaError_t gemm_prepare_device() {
   cudaError_t e;
+  if ((e = prepare_pair<false, EpiBiasBf16>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<false, EpiResidual>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<false, EpiGelu<false>>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<true, EpiBiasBf16>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<true, EpiResidual>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<true, EpiGelu<true>>()) != cudaSuccess) return e;
   if ((e = prepare_bn<256>()) != cudaSuccess) return e;
   if ((e = prepare_bn<192>()) != cudaSuccess) return e;
   if ((e = prepare_bn<128>()) != cudaSuccess) return e;
@@ -138,6 +193,7 @@ cudaError_t gemm_prepare_device() {
 }
 
 cudaError_t gemm_launch(const GemmPlan& plan, cudaStream_t stream) {
+  if (plan.pair) return plan.args.fp8 ? launch_pair_epi<true>(plan, stream) : launch_pair_epi<false>(plan, stream);
   return plan.args.fp8 ? launch_fp8<true>(plan, stream) : launch_fp8<false>(plan, stream);
 }
 

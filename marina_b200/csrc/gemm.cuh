@@ -430,4 +430,245 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
   }
 }
 
+// ---- the CTA-pair kernel ------------------------------------------------------------------
+// The same GEMM on 256 x 256 output tiles computed by a cluster of two CTAs with tcgen05
+// cta_group::2: each CTA loads its own 128 rows of A and 128 rows (output columns) of B into
+// its shared memory, the even CTA (leader) issues M = 256, N = 256 MMAs that read both CTAs'
+// operands, and each CTA's TMEM receives the 128 x 256 accumulator of its own rows. Per CTA a
+// stage is 32 KB (against 48 KB for the same FLOPs on one CTA), so the ring is 6 deep.
+//
+// Barriers: the leader's full[s] counts both CTAs' TMA bytes (expect_tx posted by the leader);
+// the leader's MMA commits to empty[s] and tmem_full[a] of both CTAs at once (multicast
+// commit); tmem_empty[a] lives in the leader and counts the epilogue warps of both CTAs (the
+// peer arrives remotely). Every wait is bounded as in the single-CTA kernel.
+template <int OUT_BYTES, int EPI_WARPS>
+struct PairShape {
+  static constexpr int kBN = 256;       // output columns per pair tile
+  static constexpr int kBHalf = 128;    // B rows loaded by each CTA
+  static constexpr int kABytes = kTileM * kStageRowBytes;
+  static constexpr int kBBytes = kBHalf * kStageRowBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kEpiBufBytes = 32 * kEpiChunk * OUT_BYTES;
+  static constexpr int kEpiBytes = EPI_WARPS * kEpiBufBytes;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kFit = (kMaxSmem - 1024 - kBarrierBytes - kEpiBytes) / kStageBytes;
+  static constexpr int kStages = kFit > 8 ? 8 : kFit;
+  static_assert(kStages >= 2, "not enough shared memory for a 2-stage pipeline");
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kEpiBytes + kBarrierBytes;
+  static constexpr int kThreads = 64 + 32 * EPI_WARPS;
+};
+
+template <bool FP8, class Epi>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * Epi::kWarps, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                     const __grid_constant__ CUtensorMap map_out, Epi epi, int M, int N, int K, int* status) {
+  using S = PairShape<Epi::kOutBytes, Epi::kWarps>;
+  constexpr int BN = S::kBN;
+  constexpr int kStages = S::kStages;
+  constexpr int kEpiWarps = Epi::kWarps;
+  constexpr int kEpiBufBytes = S::kEpiBufBytes;
+  constexpr int kEpiBytes = S::kEpiBytes;
+  constexpr int kElemsPerStage = FP8 ? 128 : 64;
+  constexpr uint32_t kIdesc = FP8 ? idesc_e4m3(2 * kTileM, BN) : idesc_bf16(2 * kTileM, BN);
+  constexpr int kRowBytes = kEpiChunk * Epi::kOutBytes;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm_a = smem;
+  uint8_t* sm_b = smem + kStages * S::kABytes;
+  uint8_t* sm_epi = smem + kStages * S::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm_epi + kEpiBytes);
+  uint64_t* full = bars;                     // [kStages] both CTAs' TMA -> leader's MMA (leader's copy used)
+  uint64_t* empty = bars + kStages;          // [kStages] MMA -> each CTA's producer
+  uint64_t* tmem_full = bars + 2 * kStages;  // [2] MMA -> each CTA's epilogue
+  uint64_t* tmem_empty = tmem_full + 2;      // [2] both CTAs' epilogues -> MMA (leader's copy used)
+  uint64_t* drain = tmem_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int pairs = gridDim.x >> 1;
+  const int n_tiles = N / BN;
+  const int m_tiles = (M + 2 * kTileM - 1) / (2 * kTileM);
+  const int total = m_tiles * n_tiles;
+  const int k_blocks = (K + kElemsPerStage - 1) / kElemsPerStage;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 2 * kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_barrier_init();
+    tma_prefetch_map(&map_a);
+    tma_prefetch_map(&map_b);
+    tma_prefetch_map(&map_out);
+  }
+  // Both CTAs' barriers exist before either signals the other's.
+  cluster_sync();
+  if (warp == 0) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer (both CTAs): own A rows, own half of B; bytes counted on the leader
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, parity_mask = 0;
+      for (int tile = pair; tile < total && !*abort; tile += pairs) {
+        const int m0 = (tile / n_tiles) * 2 * kTileM + static_cast<int>(rank) * kTileM;
+        const int nb = (tile % n_tiles) * BN + static_cast<int>(rank) * S::kBHalf;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort)) {
+            raise_error(status, abort, kErrTimeoutProducer);
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
+          const uint32_t bar = map_to_rank(smem_u32(&full[stage]), 0);
+          tma_load_2d_pair(sm_a + stage * S::kABytes, &map_a, bar, kb * kElemsPerStage, m0);
+          tma_load_2d_pair(sm_b + stage * S::kBBytes, &map_b, bar, kb * kElemsPerStage, nb);
+          issued_mask |= 1u << stage;
+          parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (*abort && leader) {
+        for (int s = 0; s < kStages; ++s)
+          if (issued_mask & (1u << s)) mbar_wait_bounded(&full[s], (parity_mask >> s) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---- MMA issuer (leader only)
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool issued = false;
+      for (int tile = pair; tile < total; tile += pairs) {
+        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort)) {
+          raise_error(status, abort, kErrTimeoutMma);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort)) {
+            raise_error(status, abort, kErrTimeoutMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sm_a + stage * S::kABytes);
+          const uint32_t b_addr = smem_u32(sm_b + stage * S::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kStageRowBytes / 32; ++k) {
+            const uint64_t ad = desc_sw128(a_addr + 32u * k);
+            const uint64_t bd = desc_sw128(b_addr + 32u * k);
+            if constexpr (FP8)
+              mma_pair_e4m3(d, ad, bd, kIdesc, (kb | k) != 0);
+            else
+              mma_pair_bf16(d, ad, bd, kIdesc, (kb | k) != 0);
+          }
+          issued = true;
+          tc_commit_pair(&empty[stage], 0x3);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(&tmem_full[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (*abort && issued) {
+        tc_commit_pair(drain, 0x1);
+        if (!mbar_wait_bounded(drain, 0) && status) atomicCAS(status, 0, kErrTimeoutDrain);
+      }
+    }
+  } else {
+    // ---- epilogue (both CTAs): this CTA's 128 rows x 256 columns
+    constexpr int kParts = kEpiWarps / 4;
+    const int quarter = warp & 3;
+    const int part = (warp - 2) >> 2;
+    uint8_t* sb = sm_epi + (warp - 2) * kEpiBufBytes;
+    const uint32_t empty_addr0 = map_to_rank(smem_u32(&tmem_empty[0]), 0);
+    const uint32_t empty_addr1 = map_to_rank(smem_u32(&tmem_empty[1]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < total; tile += pairs) {
+      const int m0 = (tile / n_tiles) * 2 * kTileM + static_cast<int>(rank) * kTileM;
+      const int n0 = (tile % n_tiles) * BN;
+      if (!mbar_wait(&tmem_full[acc], acc_phase, abort)) {
+        if (lane == 0) raise_error(status, abort, kErrTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const int row0 = m0 + quarter * 32;
+#pragma unroll 1
+      for (int c = part * kEpiChunk; c < BN; c += kParts * kEpiChunk) {
+        float v[32];
+        tmem_ld32(taddr + c, v);
+        if (c + kParts * kEpiChunk >= BN) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(acc ? empty_addr1 : empty_addr0);
+        }
+        uint4 out[Epi::kOutBytes * 2];
+        epi.pack(n0 + c, v, out);
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < Epi::kOutBytes * 2; ++j)
+          *reinterpret_cast<uint4*>(sb + staged_offset<kRowBytes>(lane, j)) = out[j];
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          if (row0 < M) {
+            if constexpr (Epi::kReduce)
+              tma_reduce_add_2d(&map_out, sb, n0 + c, row0);
+            else
+              tma_store_2d(&map_out, sb, n0 + c, row0);
+          }
+          bulk_commit();
+        }
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  // Neither CTA leaves (or frees TMEM) while the other may still signal its barriers.
+  cluster_sync();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kTmemCols);
+  }
+}
+
 }  // namespace mrn

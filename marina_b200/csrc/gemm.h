@@ -36,9 +36,11 @@ struct GemmPlan {
   GemmArgs args;
   int bn = 0;
   int grid = 0;
+  bool pair = false;  // 256 x 256 tiles on CTA pairs (tcgen05 cta_group::2)
 };
 
-// Widest supported N tile (256, 192, 128, 64) dividing n; 0 if none.
+// Widest supported N tile (256, 192, 128, 64) dividing n; 0 if none. Plans for N a multiple of
+// 256 run on CTA pairs unless the environment sets MRN_GEMM_PAIR=0.
 int gemm_pick_bn(int n);
 
 // Validate shapes and alignment and build the tensor maps. `err` (>= 256 bytes) receives a
