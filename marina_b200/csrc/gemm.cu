@@ -144,7 +144,9 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
     snprintf(err, 256, "gemm: output/bias misaligned or ldo %d < N %d", args.ldo, args.n);
     return false;
   }
-  plan->pair = pair_enabled() && args.n % 256 == 0;
+  // CTA pairs halve the operand bytes per FLOP, which pays where the main loop is long (FFN2,
+  // K = 4d); with K = d the two CTAs' coupled epilogues cost more than that saves.
+  plan->pair = pair_enabled() && args.n % 256 == 0 && args.k >= 1024;
   if (!make_kmajor_map(&plan->map_a, args.a, eb, args.m, args.k, kTileM) ||
       !make_kmajor_map(&plan->map_b, args.b, eb, args.n, args.k, plan->pair ? 128 : plan->bn)) {
     snprintf(err, 256, "gemm: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", args.m, args.n, args.k);

@@ -40,7 +40,7 @@ struct GemmPlan {
 };
 
 // Widest supported N tile (256, 192, 128, 64) dividing n; 0 if none. Plans for N a multiple of
-// 256 run on CTA pairs unless the environment sets MRN_GEMM_PAIR=0.
+// 256 and K >= 1024 run on CTA pairs unless the environment sets MRN_GEMM_PAIR=0.
 int gemm_pick_bn(int n);
 
 // Validate shapes and alignment and build the tensor maps. `err` (>= 256 bytes) receives a

@@ -19,6 +19,8 @@ SHAPES = [
     (65 * 3, 576, 192), (65 * 3, 192, 192), (65 * 3, 768, 192), (65 * 3, 192, 768),
     (65 * 7, 1536, 512), (65 * 7, 512, 512), (65 * 7, 2048, 512), (65 * 7, 512, 2048),
     (1, 256, 64), (128, 128, 128), (65 * 64, 1536, 512),
+    # CTA-pair tiles (N % 256 == 0, K >= 1024): one, two and ragged 256-row blocks
+    (65 * 3, 512, 1024), (130, 256, 1024), (65 * 9, 512, 2048), (1, 256, 1024),
 ]
 
 
