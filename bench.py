@@ -296,12 +296,17 @@ def run_ours(args):
     prof = net.profile(B, d_boards.data_ptr(), d_legal.data_ptr(), d_priors.data_ptr(), d_wdl.data_ptr(),
                        stream.cuda_stream)
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-    bf16_peak = peaks.get("bf16_tflops")
+    # The profiled pass runs right after the timed steps (over a second of continuous work, at the
+    # power cap), so the sustained cuBLAS figure is the denominator; e4m3 doubles it because the
+    # file carries no FP8 figure.
+    bf16_peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
+    kind = "sustained" if peaks.get("bf16_tflops_sustained") else "burst"
     if bf16_peak:
-        peak, peak_src = (2 * bf16_peak, "2x measured bf16 burst (MEASURED_PEAKS.json has no fp8 figure)") \
-            if args.precision == "fp8" else (bf16_peak, "measured bf16 burst (MEASURED_PEAKS.json)")
+        peak, peak_src = (2 * bf16_peak, f"2x measured bf16 {kind} (MEASURED_PEAKS.json has no fp8 figure)") \
+            if args.precision == "fp8" else (bf16_peak, f"measured bf16 {kind} (MEASURED_PEAKS.json)")
     else:
-        peak, peak_src = (2 * 1590.0, "2x fallback bf16") if args.precision == "fp8" else (1590.0, "fallback bf16")
+        peak, peak_src = (2 * 1400.0, "2x fallback bf16 sustained") if args.precision == "fp8" \
+            else (1400.0, "fallback bf16 sustained")
     g = prof["gemm"]
     achieved = g["flops"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else 0.0
     total_prof_ms = sum(v["ms"] for v in prof.values())
