@@ -62,59 +62,93 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return r;
 }
 
-// GELU(x) = x * Phi(x), Phi(x) = 0.5 (1 + erf(x / sqrt 2)), with erf from Abramowitz & Stegun
-// 7.1.28: erf(z) = 1 - (1 + a1 z + ... + a6 z^6)^-16 for z >= 0, |error| <= 3e-7. One
-// hardware reciprocal and a dozen FMA-pipe operations per element (the epilogue of FFN1
-// evaluates it for every one of the R x d_ff hidden activations). The coefficients below are
-// a_k * 2^(1/16), so the 16th power carries the factor 2 and its reciprocal is directly
-// 0.5 (1 - erf(z)), the upper tail of Phi at |x|. z is clamped at 10, where erf is 1 in f32
-// and the 16th power stays finite.
-constexpr float kTwoPow16th = 1.0442737824274138f;  // 2^(1/16)
-constexpr float kErfC0 = 1.0f * kTwoPow16th;
-constexpr float kErfC1 = 0.0705230784f * kTwoPow16th;
-constexpr float kErfC2 = 0.0422820123f * kTwoPow16th;
-constexpr float kErfC3 = 0.0092705272f * kTwoPow16th;
-constexpr float kErfC4 = 0.0001520143f * kTwoPow16th;
-constexpr float kErfC5 = 0.0002765672f * kTwoPow16th;
-constexpr float kErfC6 = 0.0000430638f * kTwoPow16th;
-
-__device__ __forceinline__ float gelu_erf(float x) {
-  const float z = fminf(fabsf(x) * 0.70710678118654752f, 10.f);
-  float p = fmaf(z, kErfC6, kErfC5);
-  p = fmaf(z, p, kErfC4);
-  p = fmaf(z, p, kErfC3);
-  p = fmaf(z, p, kErfC2);
-  p = fmaf(z, p, kErfC1);
-  p = fmaf(z, p, kErfC0);
-  p = p * p;  // ^2
-  p = p * p;  // ^4
-  p = p * p;  // ^8
-  p = p * p;  // ^16 (times 2)
-  const float q = rcp_approx(p);
-  return x * (x >= 0.f ? 1.f - q : q);
+// Two f32 lanes at once: d = a * b + c (the packed f32 FMA of sm_100).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 pa, pb, pc, pd;\n\t"
+      "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\tmov.b64 pc, {%6, %7};\n\t"
+      "fma.rn.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
 }
 
-// The same on two values in packed f16 arithmetic, for outputs that are rounded to e4m3
-// (3 mantissa bits) right after: f16 keeps the result well inside one e4m3 step, at about half
-// the instructions. Where the 16th power overflows f16 (|x| > ~4.2, erf(z) > 1 - 2e-5) the
-// reciprocal is 0 and Phi is 0 or 1.
-__device__ __forceinline__ __half2 gelu_erf_h2(__half2 x) {
-  const __half2 z = __hmul2(__habs2(x), __float2half2_rn(0.70710678118654752f));
-  __half2 p = __hfma2(z, __float2half2_rn(kErfC6), __float2half2_rn(kErfC5));
-  p = __hfma2(z, p, __float2half2_rn(kErfC4));
-  p = __hfma2(z, p, __float2half2_rn(kErfC3));
-  p = __hfma2(z, p, __float2half2_rn(kErfC2));
-  p = __hfma2(z, p, __float2half2_rn(kErfC1));
-  p = __hfma2(z, p, __float2half2_rn(kErfC0));
-  p = __hmul2(p, p);
-  p = __hmul2(p, p);
-  p = __hmul2(p, p);
-  p = __hmul2(p, p);
-  const __half2 q = h2rcp(p);
-  // Phi = q + [x >= 0] (1 - 2q)
-  const __half2 ge = __hge2(x, __float2half2_rn(0.f));
-  const __half2 phi = __hfma2(ge, __hfma2(q, __float2half2_rn(-2.f), __float2half2_rn(1.f)), q);
-  return __hmul2(x, phi);
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ __half2 ex2_approx_h2(__half2 x) {
+  uint32_t r;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(*reinterpret_cast<const uint32_t*>(&x)));
+  return *reinterpret_cast<const __half2*>(&r);
+}
+
+// (lo, hi) -> f16x2, saturating to +-65504 instead of overflowing to infinity.
+__device__ __forceinline__ __half2 f32x2_to_h2_sat(float2 v) {
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(v.y), "f"(v.x));
+  return *reinterpret_cast<const __half2*>(&r);
+}
+
+// Exact GELU, x Phi(x) with Phi the standard normal CDF (torch.nn.GELU(); the reference's
+// gelu_exact, src/net/cuda/kernels.cu:62-65), written as
+//
+//     GELU(x) = relu(x) - |x| Phi(-|x|),    Phi(-a) = 2^(-g(a)),   g(a) = -log2 Phi(-a),
+//
+// so an element costs one hardware exponential (ex2) plus a polynomial for g, which is smooth
+// and convex on a >= 0. The coefficients (negated, so the Horner chain gives -g) are
+// least-squares fits on Chebyshev nodes made by gelu_fit.py beside this file; a is clamped
+// at the fit's bound, past which Phi(-a) no longer moves the output by half an ulp.
+//   f32 form (bf16 outputs): degree 7, |relative GELU error| <= 4.3e-6.
+//   packed f16 form (outputs rounded to e4m3 next, 12.5% steps): degree 5, <= 1.1e-2,
+//   most of it the f16 rounding of x itself.
+// kGeluF32: degree 7 on [0, 5.5], max relative GELU error 4.21e-06 in float32
+constexpr float kGeluF32Bound = 5.5f;
+constexpr float kGeluF32_0 = -9.999938561e-01f;
+constexpr float kGeluF32_1 = -1.151278331e+00f;
+constexpr float kGeluF32_2 = -4.583817849e-01f;
+constexpr float kGeluF32_3 = -5.405228293e-02f;
+constexpr float kGeluF32_4 = 8.556272268e-03f;
+constexpr float kGeluF32_5 = -9.434208502e-04f;
+constexpr float kGeluF32_6 = 6.328849712e-05f;
+constexpr float kGeluF32_7 = -1.921234625e-06f;
+// kGeluF16: degree 5 on [0, 5.0], max relative GELU error 1.11e-02 in float16
+constexpr float kGeluF16Bound = 5.0f;
+constexpr float kGeluF16_0 = -1.000238752e+00f;
+constexpr float kGeluF16_1 = -1.147657292e+00f;
+constexpr float kGeluF16_2 = -4.671405841e-01f;
+constexpr float kGeluF16_3 = -4.618088635e-02f;
+constexpr float kGeluF16_4 = 5.264457609e-03f;
+constexpr float kGeluF16_5 = -2.672135067e-04f;
+
+// GELU of two f32 values, packed arithmetic for the polynomial.
+__device__ __forceinline__ float2 gelu2(float2 x) {
+  const float2 a = make_float2(fabsf(x.x), fabsf(x.y));
+  const float2 t = make_float2(fminf(a.x, kGeluF32Bound), fminf(a.y, kGeluF32Bound));
+  float2 p = fma2(t, make_float2(kGeluF32_7, kGeluF32_7), make_float2(kGeluF32_6, kGeluF32_6));
+  p = fma2(t, p, make_float2(kGeluF32_5, kGeluF32_5));
+  p = fma2(t, p, make_float2(kGeluF32_4, kGeluF32_4));
+  p = fma2(t, p, make_float2(kGeluF32_3, kGeluF32_3));
+  p = fma2(t, p, make_float2(kGeluF32_2, kGeluF32_2));
+  p = fma2(t, p, make_float2(kGeluF32_1, kGeluF32_1));
+  p = fma2(t, p, make_float2(kGeluF32_0, kGeluF32_0));
+  const float2 q = make_float2(ex2_approx(p.x), ex2_approx(p.y));  // Phi(-|x|)
+  return fma2(make_float2(-a.x, -a.y), q, make_float2(fmaxf(x.x, 0.f), fmaxf(x.y, 0.f)));
+}
+
+// The same on a packed f16 pair.
+__device__ __forceinline__ __half2 gelu_h2(__half2 x) {
+  const __half2 a = __habs2(x);
+  const __half2 t = __hmin2(a, __float2half2_rn(kGeluF16Bound));
+  __half2 p = __hfma2(t, __float2half2_rn(kGeluF16_5), __float2half2_rn(kGeluF16_4));
+  p = __hfma2(t, p, __float2half2_rn(kGeluF16_3));
+  p = __hfma2(t, p, __float2half2_rn(kGeluF16_2));
+  p = __hfma2(t, p, __float2half2_rn(kGeluF16_1));
+  p = __hfma2(t, p, __float2half2_rn(kGeluF16_0));
+  const __half2 q = ex2_approx_h2(p);
+  return __hfma2(__hneg2(a), q, __hmax2(x, __float2half2_rn(0.f)));
 }
 
 // Byte offset of 16-byte chunk `j` of row `r` in a staging block whose rows are RB bytes and
@@ -139,16 +173,14 @@ struct EpiBiasBf16 {
   const float* bias;
   float scale;
   __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[4]) const {
+    const float2 s2 = make_float2(scale, scale);
 #pragma unroll
-    for (int c = 0; c < 32; c += 8) {
-      const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + col + c));
-      const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + col + c + 4));
-      __nv_bfloat162 p[4];
-      p[0] = __floats2bfloat162_rn(v[c + 0] * scale + b0.x, v[c + 1] * scale + b0.y);
-      p[1] = __floats2bfloat162_rn(v[c + 2] * scale + b0.z, v[c + 3] * scale + b0.w);
-      p[2] = __floats2bfloat162_rn(v[c + 4] * scale + b1.x, v[c + 5] * scale + b1.y);
-      p[3] = __floats2bfloat162_rn(v[c + 6] * scale + b1.z, v[c + 7] * scale + b1.w);
-      o[c / 8] = *reinterpret_cast<const uint4*>(p);
+    for (int c = 0; c < 32; c += 4) {
+      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c));
+      const float2 y0 = fma2(make_float2(v[c], v[c + 1]), s2, make_float2(b.x, b.y));
+      const float2 y1 = fma2(make_float2(v[c + 2], v[c + 3]), s2, make_float2(b.z, b.w));
+      __nv_bfloat162 p[2] = {__floats2bfloat162_rn(y0.x, y0.y), __floats2bfloat162_rn(y1.x, y1.y)};
+      reinterpret_cast<uint2*>(o)[c / 4] = *reinterpret_cast<const uint2*>(p);
     }
   }
 };
@@ -164,6 +196,7 @@ struct EpiGelu {
   float scale;
   float inv_q;
   __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[kOutBytes * 2]) const {
+    const float2 s2 = make_float2(scale, scale);
     if constexpr (E4M3) {
       const __half2 iq = __float2half2_rn(inv_q);
 #pragma unroll
@@ -172,10 +205,10 @@ struct EpiGelu {
 #pragma unroll
         for (int j = 0; j < 8; j += 2) {
           const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c + 2 * j));
-          const __half2 x0 = __floats2half2_rn(v[c + 2 * j] * scale + b.x, v[c + 2 * j + 1] * scale + b.y);
-          const __half2 x1 = __floats2half2_rn(v[c + 2 * j + 2] * scale + b.z, v[c + 2 * j + 3] * scale + b.w);
-          const __half2 y0 = __hmul2(gelu_erf_h2(x0), iq);
-          const __half2 y1 = __hmul2(gelu_erf_h2(x1), iq);
+          const float2 x0 = fma2(make_float2(v[c + 2 * j], v[c + 2 * j + 1]), s2, make_float2(b.x, b.y));
+          const float2 x1 = fma2(make_float2(v[c + 2 * j + 2], v[c + 2 * j + 3]), s2, make_float2(b.z, b.w));
+          const __half2 y0 = __hmul2(gelu_h2(f32x2_to_h2_sat(x0)), iq);
+          const __half2 y1 = __hmul2(gelu_h2(f32x2_to_h2_sat(x1)), iq);
           q[j] = __nv_cvt_halfraw2_to_fp8x2(y0, __NV_SATFINITE, __NV_E4M3);
           q[j + 1] = __nv_cvt_halfraw2_to_fp8x2(y1, __NV_SATFINITE, __NV_E4M3);
         }
@@ -183,15 +216,12 @@ struct EpiGelu {
       }
     } else {
 #pragma unroll
-      for (int c = 0; c < 32; c += 8) {
-        const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + col + c));
-        const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + col + c + 4));
-        __nv_bfloat162 p[4];
-        p[0] = __floats2bfloat162_rn(gelu_erf(v[c + 0] * scale + b0.x), gelu_erf(v[c + 1] * scale + b0.y));
-        p[1] = __floats2bfloat162_rn(gelu_erf(v[c + 2] * scale + b0.z), gelu_erf(v[c + 3] * scale + b0.w));
-        p[2] = __floats2bfloat162_rn(gelu_erf(v[c + 4] * scale + b1.x), gelu_erf(v[c + 5] * scale + b1.y));
-        p[3] = __floats2bfloat162_rn(gelu_erf(v[c + 6] * scale + b1.z), gelu_erf(v[c + 7] * scale + b1.w));
-        o[c / 8] = *reinterpret_cast<const uint4*>(p);
+      for (int c = 0; c < 32; c += 4) {
+        const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c));
+        const float2 y0 = gelu2(fma2(make_float2(v[c], v[c + 1]), s2, make_float2(b.x, b.y)));
+        const float2 y1 = gelu2(fma2(make_float2(v[c + 2], v[c + 3]), s2, make_float2(b.z, b.w)));
+        __nv_bfloat162 p[2] = {__floats2bfloat162_rn(y0.x, y0.y), __floats2bfloat162_rn(y1.x, y1.y)};
+        reinterpret_cast<uint2*>(o)[c / 4] = *reinterpret_cast<const uint2*>(p);
       }
     }
   }
@@ -205,12 +235,13 @@ struct EpiResidual {
   const float* bias;
   float scale;
   __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[8]) const {
+    const float2 s2 = make_float2(scale, scale);
 #pragma unroll
     for (int c = 0; c < 32; c += 4) {
       const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c));
-      float4 r = make_float4(v[c + 0] * scale + b.x, v[c + 1] * scale + b.y, v[c + 2] * scale + b.z,
-                             v[c + 3] * scale + b.w);
-      o[c / 4] = *reinterpret_cast<const uint4*>(&r);
+      const float2 y0 = fma2(make_float2(v[c], v[c + 1]), s2, make_float2(b.x, b.y));
+      const float2 y1 = fma2(make_float2(v[c + 2], v[c + 3]), s2, make_float2(b.z, b.w));
+      o[c / 4] = make_uint4(__float_as_uint(y0.x), __float_as_uint(y0.y), __float_as_uint(y1.x), __float_as_uint(y1.y));
     }
   }
 };

@@ -23,6 +23,7 @@ enum DeviceError : int {
   kErrTimeoutMma = 2,
   kErrTimeoutEpilogue = 3,
   kErrTimeoutDrain = 4,
+  kErrTimeoutExchange = 5,  // a row-statistics exchange between the CTAs of a cluster
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -220,6 +221,59 @@ __device__ __forceinline__ void cluster_sync() {
 // Arrive on an mbarrier in another CTA of the cluster (address from map_to_rank).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// This CTA's cluster index, the number of clusters in the grid, and CTAs per cluster.
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
+// Store one f32 into the shared memory of a CTA of the cluster (address from map_to_rank).
+__device__ __forceinline__ void st_cluster_f32(uint32_t cluster_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
+// Bounded wait on a local mbarrier whose arrivals come from other CTAs of the cluster
+// (acquire at cluster scope, so their stores before arriving are visible afterwards).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait_cluster(a, parity)) return true;
+  const unsigned long long start = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(a, parity)) return true;
+    if ((i & 31u) == 0) {
+      if (*abort) return false;
+      if (globaltimer() - start > kWaitLimitNs) return false;
+    }
+  }
+}
+
+// Named barrier over `threads` threads (a multiple of 32) of this CTA; id 0 is __syncthreads.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // TMA tile load into this CTA's shared memory whose completion bytes are counted on the
