@@ -56,7 +56,9 @@ typedef enum mrn_status {
 
 /* Arithmetic of the linear layers. */
 typedef enum mrn_precision {
-  /* bf16 weights and activations on tcgen05 kind::f16, f32 accumulation and residual stream. */
+  /* bf16 weights and activations on tcgen05 kind::f16, f32 accumulation. In every precision the
+   * residual stream is f16 (each residual add computed in f32 and rounded to f16), as in the
+   * reference's CUDA backend (src/net/cuda/mod.rs:1-2, :193). */
   MRN_PRECISION_BF16 = 0,
   /* Weights quantised to e4m3 with one scale per matrix (src/net/cuda/mod.rs:376-405),
    * activations bf16: the e4m3 codes run on kind::f16 exactly, the scale is applied in the
@@ -190,7 +192,7 @@ MRN_API void mrn_destroy(mrn_ctx* ctx);
  * not stall on an allocation, a device that is already full). It allocates nothing: all
  * intermediate buffers live in one 8 MiB array compiled into the library, resident on every
  * GPU that loads it for the life of the process. Batches are limited to what fits that array
- * (11 positions for the `small` network in bf16/fp8w, 15 in fp8; 30 / 41 for `nano`); larger
+ * (12 positions for the `small` network in bf16/fp8w, 17 in fp8; 33 / 47 for `nano`); larger
  * ones return MRN_ERR_BATCH_TOO_LARGE. Inputs and outputs are the caller's device buffers, as
  * for `mrn_evaluate_device`. Every call on a device shares the array, so calls whose GPU work
  * overlaps (other streams, other contexts on the same device) corrupt each other's results:
@@ -203,7 +205,7 @@ MRN_API int mrn_evaluate_device_static(mrn_ctx* ctx, int n, const uint8_t* d_boa
 
 /* One GEMM launch: out = epilogue(a[m,k] . b[n,k]^T * scale + bias). `fp8` selects e4m3
  * operands; `epilogue` is 0 bias->bf16, 1 GELU->bf16, 2 GELU->e4m3 (x inv_q), 3 residual
- * add into f32. */
+ * add into f16 `out`. */
 MRN_API int mrn_test_gemm(int fp8, int epilogue, const void* a, const void* b, const float* bias, void* out, int ldo, int m,
                   int n, int k, float scale, float inv_q, int* status, void* stream);
 MRN_API const char* mrn_test_last_error(void);

@@ -162,7 +162,7 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
       out_ok = make_store_map(&plan->map_out, args.out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, args.m, args.n, args.ldo);
       break;
     case Epilogue::kResidual:
-      out_ok = make_store_map(&plan->map_out, args.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, args.m, args.n, args.ldo);
+      out_ok = make_store_map(&plan->map_out, args.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.m, args.n, args.ldo);
       break;
   }
   if (!out_ok) {

@@ -2,7 +2,7 @@
 //
 //     D[M, N] = A[M, K] · B[N, K]^T        (A = activations, B = a Linear's weight, both K-major)
 //
-// followed by a fused epilogue (bias, GELU, residual add, re-quantisation). One CTA per SM
+// followed by a fused epilogue (bias, GELU, residual add into the f16 stream, re-quantisation). One CTA per SM
 // walks the output tiles (128 rows x BN columns) in n-fastest order, so the CTAs working on
 // the same 128-row block of A at the same time share it through L2.
 //
@@ -227,21 +227,22 @@ struct EpiGelu {
   }
 };
 
-// x += acc * scale + bias (the f32 residual stream), as a TMA reduce-add of the f32 values.
+// x += acc * scale + bias on the f16 residual stream, as a TMA reduce-add of the f16 values.
 struct EpiResidual {
-  static constexpr int kOutBytes = 4;
+  static constexpr int kOutBytes = 2;
   static constexpr bool kReduce = true;
   static constexpr int kWarps = 8;
   const float* bias;
   float scale;
-  __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[8]) const {
+  __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[4]) const {
     const float2 s2 = make_float2(scale, scale);
 #pragma unroll
     for (int c = 0; c < 32; c += 4) {
       const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c));
       const float2 y0 = fma2(make_float2(v[c], v[c + 1]), s2, make_float2(b.x, b.y));
       const float2 y1 = fma2(make_float2(v[c + 2], v[c + 3]), s2, make_float2(b.z, b.w));
-      o[c / 4] = make_uint4(__float_as_uint(y0.x), __float_as_uint(y0.y), __float_as_uint(y1.x), __float_as_uint(y1.y));
+      __half2 h[2] = {__floats2half2_rn(y0.x, y0.y), __floats2half2_rn(y1.x, y1.y)};
+      reinterpret_cast<uint2*>(o)[c / 4] = *reinterpret_cast<const uint2*>(h);
     }
   }
 };

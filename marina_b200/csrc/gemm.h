@@ -12,7 +12,7 @@ enum class Epilogue : int {
   kBias = 0,       // out bf16 = acc*scale + bias                  (QKV projection)
   kGeluBf16 = 1,   // out bf16 = GELU(acc*scale + bias)            (FFN1, bf16 activations)
   kGeluE4m3 = 2,   // out e4m3 = GELU(acc*scale + bias) * inv_q    (FFN1, FP8 activations)
-  kResidual = 3,   // x f32 += acc*scale + bias                    (out-proj, FFN2)
+  kResidual = 3,   // x f16 += acc*scale + bias                    (out-proj, FFN2)
 };
 
 struct GemmArgs {
@@ -21,7 +21,7 @@ struct GemmArgs {
   int m = 0, n = 0, k = 0;
   bool fp8 = false;          // operands are e4m3 (kind::f8f6f4) instead of bf16 (kind::f16)
   Epilogue epi = Epilogue::kBias;
-  void* out = nullptr;       // bf16 / e4m3 output, or the f32 residual stream
+  void* out = nullptr;       // bf16 / e4m3 output, or the f16 residual stream
   int ldo = 0;               // row stride of `out` in elements
   const float* bias = nullptr;  // [N]
   float scale = 1.f;         // dequantisation of the accumulator (weight scale x activation scale)

@@ -2,7 +2,10 @@
 // LayerNorm, per-(position, head) attention on the tensor cores, the legal-move policy head
 // and the value head's output layer. See kernels.cuh for the data layout.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_fp8.h>
+
+#include <type_traits>
 
 #include "kernels.cuh"
 
@@ -44,6 +47,40 @@ struct WarpRow {
       } else {
         const float2 q = *reinterpret_cast<const float2*>(src + col(c, lane));
         v[c * 2 + 0] = q.x, v[c * 2 + 1] = q.y;
+      }
+    }
+  }
+
+  // The same from / to the f16 residual stream.
+  __device__ __forceinline__ void load(const __half* __restrict__ src, int lane) {
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      if constexpr (VEC == 4) {
+        const uint2 q = *reinterpret_cast<const uint2*>(src + col(c, lane));
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&q.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&q.y));
+        v[c * 4 + 0] = a.x, v[c * 4 + 1] = a.y, v[c * 4 + 2] = b.x, v[c * 4 + 3] = b.y;
+      } else {
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(src + col(c, lane)));
+        v[c * 2 + 0] = a.x, v[c * 2 + 1] = a.y;
+      }
+    }
+  }
+
+  // Round every value to f16 in place (what a store to the residual stream keeps).
+  __device__ __forceinline__ void round_to_half() {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) v[i] = __half2float(__float2half_rn(v[i]));
+  }
+
+  __device__ __forceinline__ void store(__half* __restrict__ dst, int lane) const {
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      if constexpr (VEC == 4) {
+        __half2 h[2] = {__floats2half2_rn(v[c * 4], v[c * 4 + 1]), __floats2half2_rn(v[c * 4 + 2], v[c * 4 + 3])};
+        *reinterpret_cast<uint2*>(dst + col(c, lane)) = *reinterpret_cast<const uint2*>(h);
+      } else {
+        *reinterpret_cast<__half2*>(dst + col(c, lane)) = __floats2half2_rn(v[c * 2], v[c * 2 + 1]);
       }
     }
   }
@@ -161,6 +198,8 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedParams e, NormParams
 #pragma unroll
     for (int k = 0; k < VPL; ++k) r.v[k] = 0.f;
   }
+  // norm1 sees the f16 values the residual stream keeps
+  r.round_to_half();
   r.store(e.x + static_cast<size_t>(row) * d, lane);
   r.layernorm(n.gamma, n.beta, n.eps, d, lane);
   const size_t off = static_cast<size_t>(row) * d * (n.out_type == ActType::kBf16 ? 2 : 1);
@@ -168,28 +207,81 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedParams e, NormParams
 }
 
 // ---- LayerNorm, one warp per row (src/net/cpu.rs:323-343) --------------------------------
-// Warps stride over rows with gamma/beta held in registers; the next row's loads are issued
-// before the current row's reductions so every warp keeps a row of reads in flight.
+// One row of the f16 stream as loaded (VEC halves per chunk), kept packed until it is used.
 template <int VPL, int VEC>
-__global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, NormParams n, int rows, int d) {
+struct RawRow {
+  static constexpr int kChunks = VPL / VEC;
+  using Chunk = typename std::conditional<VEC == 4, uint2, uint32_t>::type;
+  Chunk c[kChunks];
+  __device__ __forceinline__ void load(const __half* __restrict__ src, int lane) {
+#pragma unroll
+    for (int k = 0; k < kChunks; ++k) c[k] = *reinterpret_cast<const Chunk*>(src + WarpRow<VPL, VEC>::col(k, lane));
+  }
+  __device__ __forceinline__ void unpack(WarpRow<VPL, VEC>& r) const {
+#pragma unroll
+    for (int k = 0; k < kChunks; ++k) {
+      const __half2* h = reinterpret_cast<const __half2*>(&c[k]);
+#pragma unroll
+      for (int e = 0; e < VEC / 2; ++e) {
+        const float2 f = __half22float2(h[e]);
+        r.v[k * VEC + 2 * e] = f.x, r.v[k * VEC + 2 * e + 1] = f.y;
+      }
+    }
+  }
+};
+
+// Warps stride over rows; gamma and beta sit in shared memory and the next three rows are in
+// flight (packed f16, VPL/2 registers each) while the current row is reduced. At 64 registers
+// a thread (d <= 512), four 256-thread blocks fit on an SM: 32 warps x 3 rows of reads
+// outstanding; wider rows get 128 registers and two blocks.
+template <int VPL>
+constexpr int ln_blocks_per_sm() {
+  return VPL > 16 ? 2 : 4;
+}
+
+template <int VPL, int VEC>
+__global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel(const __half* __restrict__ x, NormParams n, int rows, int d) {
+  extern __shared__ float gb[];  // gamma [d], beta [d]
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    gb[i] = n.gamma[i];
+    gb[d + i] = n.beta[i];
+  }
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int stride = gridDim.x * 8;
   int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
   const size_t out_bytes = n.out_type == ActType::kBf16 ? 2 : 1;
   using Row = WarpRow<VPL, VEC>;
-  Row gamma, beta, cur, nxt;
-  gamma.load(n.gamma, lane);
-  beta.load(n.beta, lane);
-  cur.load(x + static_cast<size_t>(row) * d, lane);
+  using Raw = RawRow<VPL, VEC>;
+  Raw r0, r1, r2;
+  r0.load(x + static_cast<size_t>(row) * d, lane);
+  if (row + stride < rows) r1.load(x + static_cast<size_t>(row + stride) * d, lane);
+  if (row + 2 * stride < rows) r2.load(x + static_cast<size_t>(row + 2 * stride) * d, lane);
   for (;;) {
-    const int next = row + stride;
-    if (next < rows) nxt.load(x + static_cast<size_t>(next) * d, lane);
-    cur.layernorm_regs(gamma, beta, n.eps, d);
+    Row cur;
+    r0.unpack(cur);
+    r0 = r1;
+    r1 = r2;
+    if (row + 3 * stride < rows) r2.load(x + static_cast<size_t>(row + 3 * stride) * d, lane);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) s += cur.v[i];
+    const float mean = warp_sum(s) / static_cast<float>(d);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) q += (cur.v[i] - mean) * (cur.v[i] - mean);
+    const float inv = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(d) + n.eps);
+#pragma unroll
+    for (int k = 0; k < Row::kChunks; ++k)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const int col = Row::col(k, lane) + e;
+        cur.v[k * VEC + e] = (cur.v[k * VEC + e] - mean) * inv * gb[col] + gb[d + col];
+      }
     cur.store_act(static_cast<uint8_t*>(n.out) + static_cast<size_t>(row) * d * out_bytes, n.out_type, n.inv_q, lane);
-    if (next >= rows) break;
-    row = next;
-    cur = nxt;
+    row += stride;
+    if (row >= rows) break;
   }
 }
 
@@ -554,13 +646,14 @@ struct EmbedLaunch {
 
 template <int VPL, int VEC>
 struct NormLaunch {
-  static cudaError_t run(int d, const float* x, const NormParams& n, int rows, cudaStream_t s) {
+  static cudaError_t run(int d, const __half* x, const NormParams& n, int rows, cudaStream_t s) {
     int dev = 0, sms = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int blocks_needed = (rows + 7) / 8;
-    const int grid = blocks_needed < sms * 8 ? blocks_needed : sms * 8;
-    layernorm_kernel<VPL, VEC><<<grid, 256, 0, s>>>(x, n, rows, d);
+    const int resident = sms * ln_blocks_per_sm<VPL>();
+    const int grid = blocks_needed < resident ? blocks_needed : resident;
+    layernorm_kernel<VPL, VEC><<<grid, 256, 2 * d * sizeof(float), s>>>(x, n, rows, d);
     return cudaGetLastError();
   }
 };
@@ -588,7 +681,7 @@ cudaError_t launch_embed_ln(const EmbedParams& e, const NormParams& n, int posit
   return dispatch_d<EmbedLaunch>(d, e, n, positions, s);
 }
 
-cudaError_t launch_layernorm(const float* x, const NormParams& n, int rows, int d, cudaStream_t s) {
+cudaError_t launch_layernorm(const __half* x, const NormParams& n, int rows, int d, cudaStream_t s) {
   return dispatch_d<NormLaunch>(d, x, n, rows, s);
 }
 

@@ -1,8 +1,10 @@
 // Launchers of the evaluator's non-GEMM kernels (kernels.cu). Layout: a batch of B positions
 // is R = B*t token rows (t = 65: the state token, then 64 squares), row r = pos*t + i.
-// The residual stream x is f32 [R, d]; GEMM operands are bf16 or e4m3 rows.
+// The residual stream x is f16 [R, d], as in the reference's CUDA backend (its residual adds
+// accumulate in f32 and round once to f16); GEMM operands are bf16 or e4m3 rows.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -19,7 +21,7 @@ struct EmbedParams {
   const float* castling_w;   // [d, 4]
   const float* castling_b;   // [d]
   const float* ep_embed;     // [9, d]
-  float* x;                  // [R, d]
+  __half* x;                 // [R, d]
   int t, square_start;
 };
 
@@ -35,7 +37,7 @@ struct NormParams {
 // x = tokens(boards); out = LN(x) (layer 0's norm1) in one pass.
 cudaError_t launch_embed_ln(const EmbedParams& e, const NormParams& n, int positions, int d, cudaStream_t s);
 // out = LN(x) for rows [0, rows).
-cudaError_t launch_layernorm(const float* x, const NormParams& n, int rows, int d, cudaStream_t s);
+cudaError_t launch_layernorm(const __half* x, const NormParams& n, int rows, int d, cudaStream_t s);
 
 struct AttentionParams {
   const void* qkv;   // bf16 [R, 3d]: Q | K | V, head h at columns h*hd
@@ -49,7 +51,7 @@ cudaError_t launch_attention(const AttentionParams& p, int positions, int head_d
 cudaError_t prepare_attention();
 
 struct HeadsParams {
-  const float* x;             // [R, d] residual stream after the last layer
+  const __half* x;            // [R, d] residual stream after the last layer
   const float* final_g;       // final_norm
   const float* final_b;
   const float* policy_g;      // policy_head.norm

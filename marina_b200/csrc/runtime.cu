@@ -219,7 +219,7 @@ int alloc_buffers(mrn_ctx* c) {
   const size_t B = c->max_bucket, R = B * c->t, d = c->d;
   int rc;
   if ((rc = dev_alloc(c, &c->boards, B * MRN_BOARD_BYTES)) || (rc = dev_alloc(c, &c->legal, B * MRN_MAX_LEGAL * 4)) ||
-      (rc = dev_alloc(c, &c->x, R * d * 4)) || (rc = dev_alloc(c, &c->h, R * d * c->act_bytes)) ||
+      (rc = dev_alloc(c, &c->x, R * d * 2)) || (rc = dev_alloc(c, &c->h, R * d * c->act_bytes)) ||
       (rc = dev_alloc(c, &c->qkv, R * 3 * d * 2)) || (rc = dev_alloc(c, &c->attn, R * d * c->act_bytes)) ||
       (rc = dev_alloc(c, &c->ff, R * c->dff * c->act_bytes)) || (rc = dev_alloc(c, &c->vnorm, B * d * 2)) ||
       (rc = dev_alloc(c, &c->vhid, B * d * 2)) || (rc = dev_alloc(c, &c->priors, B * MRN_MAX_LEGAL * 4)) ||

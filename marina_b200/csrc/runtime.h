@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -78,7 +79,7 @@ struct mrn_ctx {
   // activations and I/O
   uint8_t* boards = nullptr;
   int32_t* legal = nullptr;
-  float* x = nullptr;
+  __half* x = nullptr;  // residual stream [R, d], f16
   void* h = nullptr;
   __nv_bfloat16* qkv = nullptr;
   void* attn = nullptr;

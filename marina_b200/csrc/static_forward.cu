@@ -10,10 +10,10 @@
 //
 // The array holds kStaticScratchBytes (8 MiB) and is resident on every GPU that loads this
 // library, for the life of the process. How many positions fit depends on the network: one
-// position needs 65 rows of the residual stream (f32), the two GEMM inputs and the attention
+// position needs 65 rows of the residual stream (f16), the two GEMM inputs and the attention
 // output (bf16, or e4m3 for MRN_PRECISION_FP8), Q/K/V (bf16) and the FFN hidden layer, plus
-// two d-wide bf16 rows for the value head -- 0.73 MB for the `small` network in bf16 or fp8w
-// (11 positions; 15 in fp8) and 0.28 MB for `nano` (30 positions; 41 in fp8). Larger batches
+// two d-wide bf16 rows for the value head -- 0.67 MB for the `small` network in bf16 or fp8w
+// (12 positions; 17 in fp8) and 0.25 MB for `nano` (33 positions; 47 in fp8). Larger batches
 // are refused with MRN_ERR_BATCH_TOO_LARGE and a message naming the limit.
 //
 // The first call on a device looks up the array's device address (cudaGetSymbolAddress, once
@@ -55,7 +55,7 @@ Layout layout(const mrn_ctx* c, int n) {
   const size_t R = static_cast<size_t>(n) * c->t, d = c->d, ab = c->act_bytes;
   Layout l;
   l.x = 0;
-  l.h = l.x + align256(R * d * 4);
+  l.h = l.x + align256(R * d * 2);
   l.qkv = l.h + align256(R * d * ab);
   l.attn = l.qkv + align256(R * 3 * d * 2);
   l.ff = l.attn + align256(R * d * ab);
@@ -109,7 +109,7 @@ int forward(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, floa
   using mrn::ActType;
   using mrn::Epilogue;
   const Layout L = layout(c, n);
-  float* x = reinterpret_cast<float*>(base + L.x);
+  __half* x = reinterpret_cast<__half*>(base + L.x);
   void* h = base + L.h;
   __nv_bfloat16* qkv = reinterpret_cast<__nv_bfloat16*>(base + L.qkv);
   void* attn = base + L.attn;

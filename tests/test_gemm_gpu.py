@@ -89,12 +89,14 @@ def test_gelu_e4m3_epilogue(cuda, m, n, k):
 def test_residual_epilogue(cuda, fp8, m, n, k):
     a, b, af, bf, bias = _operands(m, n, k, fp8, seed=3)
     scale = 0.125 if fp8 else 1.0
-    x0 = torch.randn(m, n, device=cuda)
+    x0 = torch.randn(m, n, device=cuda).half()  # the residual stream is f16
     x = x0.clone()
     _run(fp8, EPI_RESIDUAL, a, b, bias, x, n, m, n, k, scale=scale)
-    ref = x0 + (af @ bf.T) * scale + bias
-    err = (x - ref).abs().max().item()
-    assert err <= 1e-4 * ref.abs().max().item() + 1e-5, err
+    delta = (af @ bf.T) * scale + bias
+    ref = x0.float() + delta
+    # the f16 sum of x and the f16-rounded update: at most an f16 half-ulp of each, plus the
+    # GEMM's own accumulation order where x and the update cancel
+    assert bool(((x.float() - ref).abs() <= (ref.abs() + delta.abs()) * 2 ** -10 + 1e-6).all())
 
 
 def test_rows_beyond_m_untouched(cuda):
