@@ -205,9 +205,16 @@ MRN_API int mrn_evaluate_device_static(mrn_ctx* ctx, int n, const uint8_t* d_boa
 
 /* One GEMM launch: out = epilogue(a[m,k] . b[n,k]^T * scale + bias). `fp8` selects e4m3
  * operands; `epilogue` is 0 bias->bf16, 1 GELU->bf16, 2 GELU->e4m3 (x inv_q), 3 residual
- * add into f16 `out`. */
+ * add into f16 `out` (4, the fused LayerNorm, goes through mrn_test_gemm_ln). */
 MRN_API int mrn_test_gemm(int fp8, int epilogue, const void* a, const void* b, const float* bias, void* out, int ldo, int m,
                   int n, int k, float scale, float inv_q, int* status, void* stream);
+/* One residual GEMM with the following LayerNorm fused in (the kernel that can serve out-proj ->
+ * norm2 and FFN2 -> the next norm1): x[m,d] (f16) += a[m,k] . b[d,k]^T * scale + bias, then
+ * h = LN(x) * gamma + beta (eps), as bf16, or with `fp8` (e4m3 operands) as e4m3 codes of
+ * h * inv_q. */
+MRN_API int mrn_test_gemm_ln(int fp8, const void* a, const void* b, const float* bias, const float* gamma,
+                             const float* beta, void* x, void* h, int m, int d, int k, float scale, float eps,
+                             float inv_q, int* status, void* stream);
 MRN_API const char* mrn_test_last_error(void);
 
 #ifdef __cplusplus

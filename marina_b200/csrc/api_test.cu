@@ -21,6 +21,27 @@ int num_sms() {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   return sms;
 }
+
+bool prepare() {
+  static bool prepared = false;
+  if (!prepared) {
+    if (mrn::gemm_prepare_device() != cudaSuccess) return false;
+    prepared = true;
+  }
+  return true;
+}
+
+int run(const mrn::GemmArgs& args, void* stream) {
+  mrn::GemmPlan plan;
+  char err[256];
+  if (!mrn::gemm_plan(&plan, args, num_sms(), err)) return fail(err);
+  const cudaError_t e = mrn::gemm_launch(plan, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    snprintf(g_test_error, sizeof(g_test_error), "gemm launch: %s", cudaGetErrorString(e));
+    return MRN_ERR_CUDA;
+  }
+  return MRN_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -29,11 +50,7 @@ const char* mrn_test_last_error(void) { return g_test_error; }
 
 int mrn_test_gemm(int fp8, int epilogue, const void* a, const void* b, const float* bias, void* out, int ldo, int m,
                   int n, int k, float scale, float inv_q, int* status, void* stream) {
-  static bool prepared = false;
-  if (!prepared) {
-    if (mrn::gemm_prepare_device() != cudaSuccess) return fail("gemm_prepare_device failed");
-    prepared = true;
-  }
+  if (!prepare()) return fail("gemm_prepare_device failed");
   mrn::GemmArgs args;
   args.a = a;
   args.b = b;
@@ -48,15 +65,34 @@ int mrn_test_gemm(int fp8, int epilogue, const void* a, const void* b, const flo
   args.scale = scale;
   args.inv_q = inv_q;
   args.status = status;
-  mrn::GemmPlan plan;
-  char err[256];
-  if (!mrn::gemm_plan(&plan, args, num_sms(), err)) return fail(err);
-  const cudaError_t e = mrn::gemm_launch(plan, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) {
-    snprintf(g_test_error, sizeof(g_test_error), "gemm launch: %s", cudaGetErrorString(e));
-    return MRN_ERR_CUDA;
-  }
-  return MRN_OK;
+  if (args.epi == mrn::Epilogue::kResidualLn) return fail("epilogue 4 goes through mrn_test_gemm_ln");
+  return run(args, stream);
+}
+
+int mrn_test_gemm_ln(int fp8, const void* a, const void* b, const float* bias, const float* gamma, const float* beta,
+                     void* x, void* h, int m, int d, int k, float scale, float eps, float inv_q, int* status,
+                     void* stream) {
+  if (!prepare()) return fail("gemm_prepare_device failed");
+  mrn::GemmArgs args;
+  args.a = a;
+  args.b = b;
+  args.m = m;
+  args.n = d;
+  args.k = k;
+  args.fp8 = fp8 != 0;
+  args.epi = mrn::Epilogue::kResidualLn;
+  args.out = x;
+  args.ldo = d;
+  args.bias = bias;
+  args.scale = scale;
+  args.status = status;
+  args.gamma = gamma;
+  args.beta = beta;
+  args.eps = eps;
+  args.ln_out = h;
+  args.ln_e4m3 = fp8 != 0;
+  args.ln_inv_q = inv_q;
+  return run(args, stream);
 }
 
 }  // extern "C"

@@ -4,6 +4,7 @@
 
 #include "gemm.cuh"
 #include "gemm.h"
+#include "gemm_ln.cuh"
 #include "tmap.h"
 
 namespace mrn {
@@ -107,7 +108,117 @@ cudaError_t prepare_bn() {
   return prepare_one<BN, true, EpiGelu<true>>();
 }
 
+// ---- residual GEMM + LayerNorm (gemm_ln.cuh): one cluster of n / BN CTAs per row block
+cudaLaunchConfig_t ln_config(dim3 grid, int threads, int smem, int cluster, cudaStream_t stream,
+                             cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+template <int BN, bool FP8>
+cudaError_t launch_ln_bn(const GemmPlan& p, cudaStream_t stream) {
+  using S = LnShape<BN>;
+  const GemmArgs& a = p.args;
+  const LnParams lp{a.bias, a.gamma, a.beta, static_cast<const __half*>(a.out), a.scale, a.eps, a.ln_inv_q, a.n};
+  cudaLaunchAttribute attr[1];
+  const cudaLaunchConfig_t cfg = ln_config(dim3(p.grid, 1, 1), S::kThreads, S::kSmemBytes, p.cluster, stream, attr);
+  return cudaLaunchKernelEx(&cfg, gemm_ln_kernel<BN, FP8, FP8>, p.map_a, p.map_b, p.map_out, p.map_aux, lp, a.m, a.k,
+                            a.status);
+}
+
+cudaError_t launch_ln(const GemmPlan& p, cudaStream_t stream) {
+  const bool f = p.args.fp8;
+  switch (p.bn) {
+    case 128: return f ? launch_ln_bn<128, true>(p, stream) : launch_ln_bn<128, false>(p, stream);
+    case 96: return f ? launch_ln_bn<96, true>(p, stream) : launch_ln_bn<96, false>(p, stream);
+    case 64: return f ? launch_ln_bn<64, true>(p, stream) : launch_ln_bn<64, false>(p, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// Clusters of `cluster` CTAs of this instantiation that fit on the device at once (0 if none).
+template <int BN, bool FP8>
+int ln_max_clusters(int cluster) {
+  using S = LnShape<BN>;
+  cudaLaunchAttribute attr[1];
+  const cudaLaunchConfig_t cfg = ln_config(dim3(cluster, 1, 1), S::kThreads, S::kSmemBytes, cluster, nullptr, attr);
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_ln_kernel<BN, FP8, FP8>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+int ln_max_clusters(int bn, bool fp8, int cluster) {
+  switch (bn) {
+    case 128: return fp8 ? ln_max_clusters<128, true>(cluster) : ln_max_clusters<128, false>(cluster);
+    case 96: return fp8 ? ln_max_clusters<96, true>(cluster) : ln_max_clusters<96, false>(cluster);
+    case 64: return fp8 ? ln_max_clusters<64, true>(cluster) : ln_max_clusters<64, false>(cluster);
+  }
+  return 0;
+}
+
+template <int BN>
+cudaError_t prepare_ln() {
+  cudaError_t e = cudaFuncSetAttribute(gemm_ln_kernel<BN, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       LnShape<BN>::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(gemm_ln_kernel<BN, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              LnShape<BN>::kSmemBytes);
+}
+
+bool plan_ln(GemmPlan* plan, const GemmArgs& args, char* err) {
+  const int eb = args.fp8 ? 1 : 2;
+  plan->bn = gemm_ln_pick_bn(args.n);
+  if (plan->bn == 0) {
+    snprintf(err, 256, "gemm+layernorm: no CTA slice of 128, 96 or 64 columns splits d=%d into <= %d CTAs", args.n,
+             kLnMaxCluster);
+    return false;
+  }
+  if (args.ldo != args.n || args.ln_e4m3 != args.fp8 || !args.gamma || !args.beta || !args.ln_out ||
+      (reinterpret_cast<uintptr_t>(args.gamma) & 15) != 0 || (reinterpret_cast<uintptr_t>(args.beta) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(args.ln_out) & 15) != 0) {
+    snprintf(err, 256, "gemm+layernorm: needs ldo == N, aligned gamma/beta/h, and e4m3 h exactly with e4m3 operands");
+    return false;
+  }
+  plan->cluster = args.n / plan->bn;
+  if (!make_kmajor_map(&plan->map_a, args.a, eb, args.m, args.k, kTileM) ||
+      !make_kmajor_map(&plan->map_b, args.b, eb, args.n, args.k, plan->bn) ||
+      !make_store_map(&plan->map_out, args.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.m, args.n, args.n) ||
+      !make_store_map(&plan->map_aux, args.ln_out,
+                      args.ln_e4m3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                      args.ln_e4m3 ? 1 : 2, args.m, args.n, args.n)) {
+    snprintf(err, 256, "gemm+layernorm: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", args.m, args.n, args.k);
+    return false;
+  }
+  const int fit = ln_max_clusters(plan->bn, args.fp8, plan->cluster);
+  if (fit <= 0) {
+    snprintf(err, 256, "gemm+layernorm: clusters of %d CTAs do not fit on this device", plan->cluster);
+    return false;
+  }
+  const int tiles = (args.m + kTileM - 1) / kTileM;
+  plan->grid = plan->cluster * (tiles < fit ? tiles : fit);
+  return true;
+}
+
 }  // namespace
+
+int gemm_ln_pick_bn(int n) {
+  for (int bn : {128, 96, 64})
+    if (n % bn == 0 && n / bn <= kLnMaxCluster) return bn;
+  return 0;
+}
 
 int gemm_pick_bn(int n) {
   for (int bn : {256, 192, 128, 64})
@@ -117,6 +228,16 @@ int gemm_pick_bn(int n) {
 
 bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
   plan->args = args;
+  plan->pair = false;
+  plan->cluster = 0;
+  if (args.epi == Epilogue::kResidualLn) {
+    if (args.m <= 0 || args.k <= 0 || (args.k * (args.fp8 ? 1 : 2)) % 16 != 0 ||
+        (reinterpret_cast<uintptr_t>(args.out) & 15) != 0 || (reinterpret_cast<uintptr_t>(args.bias) & 15) != 0) {
+      snprintf(err, 256, "gemm+layernorm: bad shape %dx%dx%d or misaligned x/bias", args.m, args.n, args.k);
+      return false;
+    }
+    return plan_ln(plan, args, err);
+  }
   plan->bn = gemm_pick_bn(args.n);
   const int eb = args.fp8 ? 1 : 2;
   if (args.m <= 0 || args.n <= 0 || args.k <= 0) {
@@ -164,6 +285,8 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
     case Epilogue::kResidual:
       out_ok = make_store_map(&plan->map_out, args.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.m, args.n, args.ldo);
       break;
+    case Epilogue::kResidualLn:
+      break;
   }
   if (!out_ok) {
     snprintf(err, 256, "gemm: output tensor map failed (M=%d N=%d ldo=%d)", args.m, args.n, args.ldo);
@@ -191,10 +314,14 @@ cudaError_t gemm_prepare_device() {
   if ((e = prepare_bn<256>()) != cudaSuccess) return e;
   if ((e = prepare_bn<192>()) != cudaSuccess) return e;
   if ((e = prepare_bn<128>()) != cudaSuccess) return e;
+  if ((e = prepare_ln<128>()) != cudaSuccess) return e;
+  if ((e = prepare_ln<96>()) != cudaSuccess) return e;
+  if ((e = prepare_ln<64>()) != cudaSuccess) return e;
   return prepare_bn<64>();
 }
 
 cudaError_t gemm_launch(const GemmPlan& plan, cudaStream_t stream) {
+  if (plan.args.epi == Epilogue::kResidualLn) return launch_ln(plan, stream);
   if (plan.pair) return plan.args.fp8 ? launch_pair_epi<true>(plan, stream) : launch_pair_epi<false>(plan, stream);
   return plan.args.fp8 ? launch_fp8<true>(plan, stream) : launch_fp8<false>(plan, stream);
 }

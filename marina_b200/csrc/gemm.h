@@ -13,6 +13,7 @@ enum class Epilogue : int {
   kGeluBf16 = 1,   // out bf16 = GELU(acc*scale + bias)            (FFN1, bf16 activations)
   kGeluE4m3 = 2,   // out e4m3 = GELU(acc*scale + bias) * inv_q    (FFN1, FP8 activations)
   kResidual = 3,   // x f16 += acc*scale + bias                    (out-proj, FFN2)
+  kResidualLn = 4, // kResidual, then h = LN(x)*gamma + beta       (out-proj -> norm2, FFN2 -> norm1)
 };
 
 struct GemmArgs {
@@ -27,6 +28,13 @@ struct GemmArgs {
   float scale = 1.f;         // dequantisation of the accumulator (weight scale x activation scale)
   float inv_q = 1.f;         // 1 / output quantisation scale (kGeluE4m3)
   int* status = nullptr;     // device error word (first error wins)
+  // kResidualLn only: the LayerNorm of the updated rows of `out` (N = d, ldo = d)
+  const float* gamma = nullptr;  // [N]
+  const float* beta = nullptr;   // [N]
+  float eps = 1e-5f;
+  void* ln_out = nullptr;        // h [M, N], bf16 or e4m3
+  bool ln_e4m3 = false;
+  float ln_inv_q = 1.f;          // 1 / e4m3 scale of h
 };
 
 struct GemmPlan {
@@ -37,11 +45,16 @@ struct GemmPlan {
   int bn = 0;
   int grid = 0;
   bool pair = false;  // 256 x 256 tiles on CTA pairs (tcgen05 cta_group::2)
+  CUtensorMap map_aux;  // kResidualLn: the h store map
+  int cluster = 0;      // kResidualLn: CTAs per row block (N / bn)
 };
 
 // Widest supported N tile (256, 192, 128, 64) dividing n; 0 if none. Plans for N a multiple of
 // 256 and K >= 1024 run on CTA pairs unless the environment sets MRN_GEMM_PAIR=0.
 int gemm_pick_bn(int n);
+
+// kResidualLn: the N slice of one CTA (128, 96 or 64 dividing n with n / slice <= 8); 0 if none.
+int gemm_ln_pick_bn(int n);
 
 // Validate shapes and alignment and build the tensor maps. `err` (>= 256 bytes) receives a
 // message on failure.

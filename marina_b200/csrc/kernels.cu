@@ -241,7 +241,7 @@ constexpr int ln_blocks_per_sm() {
 
 template <int VPL, int VEC>
 __global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel(const __half* __restrict__ x, NormParams n, int rows, int d) {
-  extern __shared__ float gb[];  // gamma [d], beta [d]
+  extern __shared__ __align__(16) float gb[];  // gamma [d], beta [d]
   for (int i = threadIdx.x; i < d; i += blockDim.x) {
     gb[i] = n.gamma[i];
     gb[d + i] = n.beta[i];
@@ -273,12 +273,24 @@ __global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel
     for (int i = 0; i < VPL; ++i) q += (cur.v[i] - mean) * (cur.v[i] - mean);
     const float inv = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(d) + n.eps);
 #pragma unroll
-    for (int k = 0; k < Row::kChunks; ++k)
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        const int col = Row::col(k, lane) + e;
-        cur.v[k * VEC + e] = (cur.v[k * VEC + e] - mean) * inv * gb[col] + gb[d + col];
+    for (int k = 0; k < Row::kChunks; ++k) {
+      // one vector read per chunk: consecutive lanes, consecutive 8 or 16 bytes, no bank conflict
+      float g[VEC], b[VEC];
+      const int col = Row::col(k, lane);
+      if constexpr (VEC == 4) {
+        const float4 g4 = *reinterpret_cast<const float4*>(gb + col);
+        const float4 b4 = *reinterpret_cast<const float4*>(gb + d + col);
+        g[0] = g4.x, g[1] = g4.y, g[2] = g4.z, g[3] = g4.w;
+        b[0] = b4.x, b[1] = b4.y, b[2] = b4.z, b[3] = b4.w;
+      } else {
+        const float2 g2 = *reinterpret_cast<const float2*>(gb + col);
+        const float2 b2 = *reinterpret_cast<const float2*>(gb + d + col);
+        g[0] = g2.x, g[1] = g2.y;
+        b[0] = b2.x, b[1] = b2.y;
       }
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) cur.v[k * VEC + e] = (cur.v[k * VEC + e] - mean) * inv * g[e] + b[e];
+    }
     cur.store_act(static_cast<uint8_t*>(n.out) + static_cast<size_t>(row) * d * out_bytes, n.out_type, n.inv_q, lane);
     row += stride;
     if (row >= rows) break;

@@ -236,37 +236,88 @@ int alloc_buffers(mrn_ctx* c) {
   return MRN_OK;
 }
 
-// GEMM plans of one bucket: per layer QKV, out-proj, FFN1, FFN2; then value ff1.
-int make_plans(mrn_ctx* c, Bucket& b) {
-  const int M = b.positions * c->t, d = c->d, ff = c->dff;
+}  // namespace
+
+namespace mrn {
+
+bool ln_fusion_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("MRN_GEMM_LN");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
+void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool fuse, GemmArgs (&g)[4]) {
+  const int d = c->d, ff = c->dff;
   const bool fp8 = c->precision == MRN_PRECISION_FP8;
+  const DevLayer& D = c->dl[l];
+  auto scale = [&](int i) { return fp8 ? D.ws[i] * D.as[i] : D.ws[i]; };
+  GemmArgs base;
+  base.m = rows;
+  base.fp8 = fp8;
+  base.status = c->status;
+  base.eps = c->eps;
+  base.ln_e4m3 = fp8;
+  for (GemmArgs& a : g) a = base;
+  // QKV: h -> qkv (bf16)
+  g[0].a = b.h, g[0].b = D.w_qkv, g[0].n = 3 * d, g[0].k = d, g[0].epi = Epilogue::kBias, g[0].out = b.qkv;
+  g[0].ldo = 3 * d, g[0].bias = D.b_qkv, g[0].scale = scale(0);
+  // out-proj: attn -> x += (then h = norm2(x))
+  g[1].a = b.attn, g[1].b = D.w_o, g[1].n = d, g[1].k = d, g[1].epi = Epilogue::kResidual, g[1].out = b.x;
+  g[1].ldo = d, g[1].bias = D.b_o, g[1].scale = scale(1);
+  if (fuse) {
+    g[1].epi = Epilogue::kResidualLn, g[1].gamma = D.n2g, g[1].beta = D.n2b, g[1].ln_out = b.h;
+    g[1].ln_inv_q = 1.f / D.as[2];
+  }
+  // FFN1: h -> ff = GELU(.)
+  g[2].a = b.h, g[2].b = D.w_1, g[2].n = ff, g[2].k = d, g[2].epi = fp8 ? Epilogue::kGeluE4m3 : Epilogue::kGeluBf16;
+  g[2].out = b.ff, g[2].ldo = ff, g[2].bias = D.b_1, g[2].scale = scale(2), g[2].inv_q = 1.f / D.as[3];
+  // FFN2: ff -> x += (then h = norm1 of the next layer)
+  g[3].a = b.ff, g[3].b = D.w_2, g[3].n = d, g[3].k = ff, g[3].epi = Epilogue::kResidual, g[3].out = b.x;
+  g[3].ldo = d, g[3].bias = D.b_2, g[3].scale = scale(3);
+  if (fuse && l + 1 < c->layers) {
+    const DevLayer& N = c->dl[l + 1];
+    g[3].epi = Epilogue::kResidualLn, g[3].gamma = N.n1g, g[3].beta = N.n1b, g[3].ln_out = b.h;
+    g[3].ln_inv_q = 1.f / N.as[0];
+  }
+}
+
+cudaError_t launch_site_layernorm(const mrn_ctx* c, int l, int site, const LayerBuffers& b, int rows,
+                                  cudaStream_t s) {
+  const DevLayer& D = c->dl[site == 0 ? l : l + 1];
+  const NormParams np = site == 0 ? NormParams{D.n2g, D.n2b, c->eps, b.h, c->act, 1.f / D.as[2]}
+                                  : NormParams{D.n1g, D.n1b, c->eps, b.h, c->act, 1.f / D.as[0]};
+  return launch_layernorm(b.x, np, rows, c->d, s);
+}
+
+}  // namespace mrn
+
+namespace {
+
+// GEMM plans of one bucket: per layer QKV, out-proj, FFN1, FFN2; then value ff1. A residual GEMM
+// whose fused LayerNorm cannot be planned on this device falls back to the plain residual
+// epilogue followed by a LayerNorm launch.
+int make_plans(mrn_ctx* c, Bucket& b) {
+  const int M = b.positions * c->t, d = c->d;
   char err[256];
+  const mrn::LayerBuffers bufs{c->h, c->qkv, c->attn, c->ff, c->x};
+  const bool fuse = mrn::ln_fusion_enabled();
+  b.fused.assign(2 * c->layers, 0);
   for (int l = 0; l < c->layers; ++l) {
-    const DevLayer& D = c->dl[l];
-    GemmArgs g;
-    g.m = M;
-    g.fp8 = fp8;
-    g.status = c->status;
-    auto scale = [&](int i) { return fp8 ? D.ws[i] * D.as[i] : D.ws[i]; };
-    // QKV: h -> qkv (bf16)
-    GemmArgs q = g;
-    q.a = c->h, q.b = D.w_qkv, q.n = 3 * d, q.k = d, q.epi = Epilogue::kBias, q.out = c->qkv, q.ldo = 3 * d;
-    q.bias = D.b_qkv, q.scale = scale(0);
-    // out-proj: attn -> x +=
-    GemmArgs o = g;
-    o.a = c->attn, o.b = D.w_o, o.n = d, o.k = d, o.epi = Epilogue::kResidual, o.out = c->x, o.ldo = d;
-    o.bias = D.b_o, o.scale = scale(1);
-    // FFN1: h -> ff = GELU(.)
-    GemmArgs f1 = g;
-    f1.a = c->h, f1.b = D.w_1, f1.n = ff, f1.k = d, f1.epi = fp8 ? Epilogue::kGeluE4m3 : Epilogue::kGeluBf16;
-    f1.out = c->ff, f1.ldo = ff, f1.bias = D.b_1, f1.scale = scale(2), f1.inv_q = 1.f / D.as[3];
-    // FFN2: ff -> x +=
-    GemmArgs f2 = g;
-    f2.a = c->ff, f2.b = D.w_2, f2.n = d, f2.k = ff, f2.epi = Epilogue::kResidual, f2.out = c->x, f2.ldo = d;
-    f2.bias = D.b_2, f2.scale = scale(3);
-    for (const GemmArgs* a : {&q, &o, &f1, &f2}) {
+    GemmArgs g[4];
+    mrn::layer_gemm_args(c, l, M, bufs, fuse, g);
+    for (int i = 0; i < 4; ++i) {
       GemmPlan p;
-      if (!mrn::gemm_plan(&p, *a, c->num_sms, err)) return c->fail(MRN_ERR_UNSUPPORTED, "layer %d: %s", l, err);
+      if (g[i].epi == Epilogue::kResidualLn) {
+        if (mrn::gemm_plan(&p, g[i], c->num_sms, err)) {
+          b.fused[2 * l + (i == 1 ? 0 : 1)] = 1;
+          b.plans.push_back(p);
+          continue;
+        }
+        g[i].epi = Epilogue::kResidual;
+      }
+      if (!mrn::gemm_plan(&p, g[i], c->num_sms, err)) return c->fail(MRN_ERR_UNSUPPORTED, "layer %d: %s", l, err);
       b.plans.push_back(p);
     }
   }
@@ -295,6 +346,7 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
   mark(MRN_PROFILE_EMBED);
   CK(mrn::launch_embed_ln(e, mrn::NormParams{D0.n1g, D0.n1b, c->eps, c->h, act, 1.f / D0.as[0]}, P, d, s));
   done();
+  const mrn::LayerBuffers bufs{c->h, c->qkv, c->attn, c->ff, c->x};
   for (int l = 0; l < c->layers; ++l) {
     const DevLayer& D = c->dl[l];
     const GemmPlan* plans = &b.plans[4 * l];
@@ -308,17 +360,18 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
     mark(MRN_PROFILE_GEMM);
     CK(mrn::gemm_launch(plans[1], s));
     done();
-    mark(MRN_PROFILE_LAYERNORM);
-    CK(mrn::launch_layernorm(c->x, mrn::NormParams{D.n2g, D.n2b, c->eps, c->h, act, 1.f / D.as[2]}, R, d, s));
-    done();
+    if (!b.fused[2 * l]) {
+      mark(MRN_PROFILE_LAYERNORM);
+      CK(mrn::launch_site_layernorm(c, l, 0, bufs, R, s));
+      done();
+    }
     mark(MRN_PROFILE_GEMM);
     CK(mrn::gemm_launch(plans[2], s));
     CK(mrn::gemm_launch(plans[3], s));
     done();
-    if (l + 1 < c->layers) {
-      const DevLayer& N = c->dl[l + 1];
+    if (l + 1 < c->layers && !b.fused[2 * l + 1]) {
       mark(MRN_PROFILE_LAYERNORM);
-      CK(mrn::launch_layernorm(c->x, mrn::NormParams{N.n1g, N.n1b, c->eps, c->h, act, 1.f / N.as[0]}, R, d, s));
+      CK(mrn::launch_site_layernorm(c, l, 1, bufs, R, s));
       done();
     }
   }
@@ -338,7 +391,13 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
   return MRN_OK;
 }
 
-int launches_per_forward(const mrn_ctx* c) { return 1 + 7 * c->layers - 1 + 3; }
+// Embedding + LayerNorm, 5 per layer (QKV, attention, out-proj, FFN1, FFN2), a LayerNorm after each
+// residual GEMM that does not carry it (norm2, and norm1 of every layer but the first), 3 for the heads.
+int launches_per_forward(const mrn_ctx* c, const Bucket& b) {
+  int n = 1 + 5 * c->layers + 3;
+  for (int l = 0; l < c->layers; ++l) n += (b.fused[2 * l] ? 0 : 1) + (l + 1 < c->layers && !b.fused[2 * l + 1]);
+  return n;
+}
 
 int get_bucket(mrn_ctx* c, int n, Bucket** out) {
   const int key = bucket_for(n);
@@ -656,7 +715,7 @@ MRN_API int mrn_profile(mrn_ctx* c, int n, const uint8_t* d_boards, const int32_
   launches[MRN_PROFILE_GEMM] = static_cast<int>(b->plans.size());
   launches[MRN_PROFILE_EMBED] = 1;
   launches[MRN_PROFILE_ATTENTION] = c->layers;
-  launches[MRN_PROFILE_LAYERNORM] = 2 * c->layers - 1;
+  launches[MRN_PROFILE_LAYERNORM] = launches_per_forward(c, *b) - (1 + 5 * c->layers + 3);
   launches[MRN_PROFILE_HEADS] = 2;
   flops[MRN_PROFILE_ATTENTION] = 4.0 * P * static_cast<double>(c->t) * c->t * c->d * c->layers;
   CK(cudaMemcpyAsync(d_priors, c->priors, static_cast<size_t>(n) * MRN_MAX_LEGAL * 4, cudaMemcpyDeviceToDevice, s));
@@ -666,8 +725,12 @@ MRN_API int mrn_profile(mrn_ctx* c, int n, const uint8_t* d_boards, const int32_
 }
 
 MRN_API int mrn_launches_per_forward(mrn_ctx* c, int n) {
-  (void)n;
-  return c ? launches_per_forward(c) : -1;
+  if (!c) return -1;
+  std::lock_guard<std::mutex> lock(c->mu);
+  if (n < 1 || n > c->max_batch) return -1;
+  Bucket* b = nullptr;
+  if (cudaSetDevice(c->device) != cudaSuccess || get_bucket(c, n, &b)) return -1;
+  return launches_per_forward(c, *b);
 }
 
 MRN_API const char* mrn_describe(mrn_ctx* c) { return c ? c->describe.c_str() : ""; }

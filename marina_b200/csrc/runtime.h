@@ -17,6 +17,8 @@
 #include "gemm.h"
 #include "kernels.cuh"
 
+struct mrn_ctx;
+
 namespace mrn {
 
 struct DevLayer {
@@ -30,7 +32,19 @@ struct DevLayer {
 struct Bucket {
   int positions = 0;
   std::vector<GemmPlan> plans;  // 4 per layer, then the value head's first layer
+  // Per layer: [2l] out-proj carries norm2, [2l+1] FFN2 carries the next layer's norm1 (the
+  // fused residual + LayerNorm epilogue); where 0, a LayerNorm launch follows the GEMM.
+  std::vector<uint8_t> fused;
   cudaGraphExec_t graph = nullptr;
+};
+
+// Buffers one forward pass runs on (the context's own, or the static scratch's).
+struct LayerBuffers {
+  void* h;
+  void* qkv;
+  void* attn;
+  void* ff;
+  __half* x;
 };
 
 // Per kernel class timing of one eager pass (mrn_profile).
@@ -112,3 +126,15 @@ struct mrn_ctx {
   }
 };
 
+namespace mrn {
+// The four GEMMs of layer `l` over `rows` rows: QKV, out-proj, FFN1, FFN2. With `fuse`, out-proj
+// carries norm2 and FFN2 (all layers but the last) the next layer's norm1 as the fused residual +
+// LayerNorm epilogue.
+void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool fuse, GemmArgs (&g)[4]);
+// Whether plans use the fused residual + LayerNorm epilogue (environment MRN_GEMM_LN=0 / 1 overrides).
+bool ln_fusion_enabled();
+// The LayerNorm launch that stands in for an unfused site: norm2 of layer `l` (site 0) or norm1 of
+// layer l + 1 (site 1), from x into h.
+cudaError_t launch_site_layernorm(const mrn_ctx* c, int l, int site, const LayerBuffers& b, int rows,
+                                  cudaStream_t s);
+}  // namespace mrn

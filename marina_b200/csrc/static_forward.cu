@@ -102,6 +102,25 @@ int gemm(mrn_ctx* c, const mrn::GemmArgs& a, cudaStream_t s) {
   return MRN_OK;
 }
 
+// A residual GEMM and the LayerNorm after it (norm2 of layer l at site 0, norm1 of layer l + 1 at
+// site 1; none after the last layer): fused where it plans, else the residual epilogue and a
+// LayerNorm launch.
+int residual(mrn_ctx* c, int l, int site, mrn::GemmArgs a, const mrn::LayerBuffers& b, cudaStream_t s) {
+  mrn::GemmPlan p;
+  char err[256];
+  if (a.epi == mrn::Epilogue::kResidualLn) {
+    if (mrn::gemm_plan(&p, a, c->num_sms, err)) {
+      CKS(mrn::gemm_launch(p, s));
+      return MRN_OK;
+    }
+    a.epi = mrn::Epilogue::kResidual;
+  }
+  if (!mrn::gemm_plan(&p, a, c->num_sms, err)) return c->fail(MRN_ERR_UNSUPPORTED, "%s", err);
+  CKS(mrn::gemm_launch(p, s));
+  if (site == 0 || l + 1 < c->layers) CKS(mrn::launch_site_layernorm(c, l, site, b, a.m, s));
+  return MRN_OK;
+}
+
 // The forward pass of the graph path (embed, layers, heads), with the array's buffers and the
 // caller's inputs and outputs.
 int forward(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, float* priors, float* wdl, uint8_t* base,
@@ -116,43 +135,26 @@ int forward(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, floa
   void* ff = base + L.ff;
   __nv_bfloat16* vnorm = reinterpret_cast<__nv_bfloat16*>(base + L.vnorm);
   __nv_bfloat16* vhid = reinterpret_cast<__nv_bfloat16*>(base + L.vhid);
-  const int R = n * c->t, d = c->d, ff_dim = c->dff;
+  const int R = n * c->t, d = c->d;
   const ActType act = c->act;
-  const bool fp8 = c->precision == MRN_PRECISION_FP8;
   int rc;
 
   const mrn::DevLayer& D0 = c->dl[0];
   CKS(mrn::launch_embed_ln(
       mrn::EmbedParams{boards, c->piece, c->square, c->state, c->cast_w, c->cast_b, c->ep, x, c->t, c->square_start},
       mrn::NormParams{D0.n1g, D0.n1b, c->eps, h, act, 1.f / D0.as[0]}, n, d, s));
+  const mrn::LayerBuffers bufs{h, qkv, attn, ff, x};
+  const bool fuse = mrn::ln_fusion_enabled();
   for (int l = 0; l < c->layers; ++l) {
     const mrn::DevLayer& D = c->dl[l];
-    auto scale = [&](int i) { return fp8 ? D.ws[i] * D.as[i] : D.ws[i]; };
-    mrn::GemmArgs g;
-    g.m = R, g.fp8 = fp8, g.status = c->status;
-    mrn::GemmArgs q = g;
-    q.a = h, q.b = D.w_qkv, q.n = 3 * d, q.k = d, q.epi = Epilogue::kBias, q.out = qkv, q.ldo = 3 * d;
-    q.bias = D.b_qkv, q.scale = scale(0);
-    if ((rc = gemm(c, q, s))) return rc;
+    mrn::GemmArgs g[4];
+    mrn::layer_gemm_args(c, l, R, bufs, fuse, g);
+    if ((rc = gemm(c, g[0], s))) return rc;
     CKS(mrn::launch_attention(mrn::AttentionParams{qkv, attn, act, 1.f / D.as[1], c->t, d, c->heads}, n,
                               d / c->heads, s));
-    mrn::GemmArgs o = g;
-    o.a = attn, o.b = D.w_o, o.n = d, o.k = d, o.epi = Epilogue::kResidual, o.out = x, o.ldo = d;
-    o.bias = D.b_o, o.scale = scale(1);
-    if ((rc = gemm(c, o, s))) return rc;
-    CKS(mrn::launch_layernorm(x, mrn::NormParams{D.n2g, D.n2b, c->eps, h, act, 1.f / D.as[2]}, R, d, s));
-    mrn::GemmArgs f1 = g;
-    f1.a = h, f1.b = D.w_1, f1.n = ff_dim, f1.k = d, f1.epi = fp8 ? Epilogue::kGeluE4m3 : Epilogue::kGeluBf16;
-    f1.out = ff, f1.ldo = ff_dim, f1.bias = D.b_1, f1.scale = scale(2), f1.inv_q = 1.f / D.as[3];
-    if ((rc = gemm(c, f1, s))) return rc;
-    mrn::GemmArgs f2 = g;
-    f2.a = ff, f2.b = D.w_2, f2.n = d, f2.k = ff_dim, f2.epi = Epilogue::kResidual, f2.out = x, f2.ldo = d;
-    f2.bias = D.b_2, f2.scale = scale(3);
-    if ((rc = gemm(c, f2, s))) return rc;
-    if (l + 1 < c->layers) {
-      const mrn::DevLayer& N = c->dl[l + 1];
-      CKS(mrn::launch_layernorm(x, mrn::NormParams{N.n1g, N.n1b, c->eps, h, act, 1.f / N.as[0]}, R, d, s));
-    }
+    if ((rc = residual(c, l, 0, g[1], bufs, s))) return rc;
+    if ((rc = gemm(c, g[2], s))) return rc;
+    if ((rc = residual(c, l, 1, g[3], bufs, s))) return rc;
   }
   mrn::HeadsParams hp;
   hp.x = x, hp.final_g = c->fn_g, hp.final_b = c->fn_b, hp.policy_g = c->pn_g, hp.policy_b = c->pn_b;

@@ -253,3 +253,51 @@ def test_device_entry_point_and_profile(nano_setup):
     expect = 2 * 64 * t * arch.n_layers * (4 * d * d + 2 * d * ff) + 2 * 64 * d * d
     assert abs(prof["gemm"]["flops"] - expect) / expect < 1e-9
     assert net.launches_per_forward(64) == 7 * arch.n_layers + 3
+
+
+FUSED_SCRIPT = r"""
+import sys, numpy as np
+from pathlib import Path
+from marina_b200 import chess, model, weights
+from marina_b200.network import B200Network
+net, precision, out = sys.argv[1], sys.argv[2], sys.argv[3]
+arch = model.Architecture.from_json((Path(model.__file__).parent / "cards" / f"{net}.json").read_text())
+w = weights.random_init(arch, seed=0)
+boards, legal, counts, _ = chess.random_positions(41, 300, 0, 120)
+ev = B200Network(arch, w, device=0, max_batch=300, precision=precision)
+p, v = ev.evaluate_packed(boards, legal)
+np.savez(out, priors=p, wdl=v, counts=counts, launches=ev.launches_per_forward(300))
+ev.close()
+"""
+
+
+@pytest.mark.parametrize("net,precision", [("small", "bf16"), ("small", "fp8"), ("nano", "fp8w")])
+def test_fused_and_unfused_layernorm_plans(tmp_path, net, precision):
+    """The residual GEMMs with the following LayerNorm fused in (MRN_GEMM_LN=1, no LayerNorm
+    launches) and the plain residual GEMM + LayerNorm launches (MRN_GEMM_LN=0) agree, and both
+    meet the oracle bounds. Child processes: the switch is read once per process."""
+    import os
+    import subprocess
+    import sys
+
+    outs = {}
+    for flag in ("0", "1"):
+        out = tmp_path / f"ln{flag}.npz"
+        env = dict(os.environ, MRN_GEMM_LN=flag)
+        subprocess.run([sys.executable, "-c", FUSED_SCRIPT, net, precision, str(out)], env=env, check=True,
+                       cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))), timeout=600)
+        outs[flag] = np.load(out)
+    layers = card(net).n_layers
+    assert int(outs["0"]["launches"]) == 7 * layers + 3 and int(outs["1"]["launches"]) == 5 * layers + 4
+    counts = outs["1"]["counts"]
+    # same arithmetic up to rounding order (one f16 rounding per residual add instead of two)
+    m = compare(outs["1"]["priors"], outs["1"]["wdl"], outs["0"]["priors"], outs["0"]["wdl"], counts)
+    print(m)
+    tight = precision != "fp8"
+    assert m["wdl"] <= (2e-3 if tight else WDL_TOL) and m["prior"] <= (2e-3 if tight else PRIOR_TOL), m
+    w = weights.random_init(card(net), seed=0)
+    boards, legal, _, _ = chess.random_positions(41, 300, 0, 120)
+    ref_p, ref_w = oracle.OracleNetwork(card(net), weights.fp8_weights(w) if precision != "bf16" else w,
+                                        threads=16).evaluate(boards, legal)
+    for flag in ("0", "1"):
+        check(compare(outs[flag]["priors"], outs[flag]["wdl"], ref_p, ref_w, counts), precision)

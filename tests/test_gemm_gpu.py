@@ -105,3 +105,73 @@ def test_rows_beyond_m_untouched(cuda):
     out = torch.full((m + 128, n), 7.0, device=cuda, dtype=torch.bfloat16)
     _run(False, EPI_BIAS, a, b, bias, out, n, m, n, k)
     assert bool((out[m:] == 7.0).all())
+
+
+def _run_ln(fp8, a, b, bias, gamma, beta, x, h, m, d, k, scale, eps, inv_q):
+    lib = _lib.load()
+    status = torch.zeros(1, dtype=torch.int32, device=a.device)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.mrn_test_gemm_ln(int(fp8), a.data_ptr(), b.data_ptr(), bias.data_ptr(), gamma.data_ptr(),
+                              beta.data_ptr(), x.data_ptr(), h.data_ptr(), m, d, k, scale, eps, inv_q,
+                              ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(stream))
+    assert rc == 0, lib.mrn_test_last_error().decode()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, f"device status {int(status.item())}"
+
+
+# (M, d, K): out-proj and FFN2 of both nets (clusters of 4 x 128 and 2 x 96 columns), ragged and
+# single-row blocks, several row blocks per cluster, and the other CTA slicings (d = 64, 256,
+# 384, 1024: clusters of 1, 2, 3, 8).
+LN_SHAPES = [
+    (65 * 7, 512, 512), (65 * 7, 512, 2048), (65 * 3, 192, 192), (65 * 3, 192, 768),
+    (1, 512, 512), (128, 512, 512), (65 * 64, 512, 2048), (65 * 256, 192, 768),
+    (65 * 5, 64, 128), (65 * 5, 256, 512), (65 * 5, 384, 384), (65 * 2, 1024, 1024),
+]
+
+
+@pytest.mark.parametrize("fp8", [False, True], ids=["bf16", "e4m3"])
+@pytest.mark.parametrize("m,d,k", LN_SHAPES)
+def test_residual_layernorm_epilogue(cuda, fp8, m, d, k):
+    """x (f16) += a.b^T*scale + bias, h = LN(x)*gamma + beta, against torch fp32 of the same op."""
+    a, b, af, bf, bias = _operands(m, d, k, fp8, seed=m + 3 * d + k)
+    g = torch.Generator(device="cuda").manual_seed(d + k)
+    gamma = 1.0 + 0.2 * torch.randn(d, device=cuda, generator=g)
+    beta = 0.1 * torch.randn(d, device=cuda, generator=g)
+    scale, eps = (0.125 if fp8 else 1.0), 1e-5
+    x0 = (torch.randn(m, d, device=cuda, generator=g) + 0.5).half()  # f16 stream, mean away from zero
+    x = torch.cat([x0, torch.full((64, d), 3.0, device=cuda, dtype=torch.float16)])  # rows past m stay
+    h = torch.full((m + 64, d), 0x55 if fp8 else 7.0, device=cuda, dtype=torch.uint8 if fp8 else torch.bfloat16)
+    q = 0.02
+    _run_ln(fp8, a, b, bias, gamma, beta, x, h, m, d, k, scale, eps, 1.0 / q)
+    delta = (af @ bf.T) * scale + bias
+    ref_x = x0.float() + delta
+    # one rounding of the f32 sum to f16, plus the accumulation-order difference of the GEMM
+    # itself (which dominates where x_old and the update cancel): the plain residual test's bound
+    assert bool(((x[:m].float() - ref_x).abs() <= (ref_x.abs() + delta.abs()) * 2 ** -10 + 1e-6).all())
+    assert bool((x[m:] == 3.0).all())
+    # h is the LayerNorm of the rows as stored in the f16 stream (checked just above)
+    ref_h = torch.nn.functional.layer_norm(x[:m].float(), (d,), gamma, beta, eps)
+    if fp8:
+        got = h[:m].view(torch.float8_e4m3fn).float() * q
+        ref_sat = ref_h.clamp(-448 * q, 448 * q)
+        assert bool(((got - ref_sat).abs() <= ref_h.abs() * 0.0625 + q * 2 ** -6 + 1e-5).all())
+        assert bool((h[m:] == 0x55).all())
+    else:
+        got = h[:m].float()
+        assert bool(((got - ref_h).abs() <= ref_h.abs() * 2 ** -8 + 1e-3).all())
+        assert bool((h[m:] == 7.0).all())
+
+
+def test_residual_layernorm_rejects_unsplittable_width(cuda):
+    """d = 160 has no 64/96/128-column CTA slice; the plan is refused, nothing is launched."""
+    m, d, k = 65, 160, 64
+    a, b, _, _, bias = _operands(m, d, k, False, seed=1)
+    ones = torch.ones(d, device=cuda)
+    x = torch.zeros(m, d, device=cuda, dtype=torch.float16)
+    h = torch.zeros(m, d, device=cuda, dtype=torch.bfloat16)
+    lib = _lib.load()
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    rc = lib.mrn_test_gemm_ln(0, a.data_ptr(), b.data_ptr(), bias.data_ptr(), ones.data_ptr(), ones.data_ptr(),
+                              x.data_ptr(), h.data_ptr(), m, d, k, 1.0, 1e-5, 1.0, ctypes.c_void_p(status.data_ptr()),
+                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc != 0 and "slice" in lib.mrn_test_last_error().decode()
