@@ -15,9 +15,10 @@
 //   warps 2..        : epilogue (8 warps, 16 for the GELU epilogue). Warp w reads TMEM lanes
 //                      32*(w%4).. (one output row per thread) in its share of the tile's
 //                      columns, 32 at a time, applies the epilogue functor, writes the
-//                      32x32 block into a swizzled shared-memory staging buffer and one lane
-//                      issues a TMA tile store (or, for the residual stream, a TMA reduce-add),
-//                      so global writes are whole swizzle rows issued by the copy engine.
+//                      32x32 block into one of its two swizzled shared-memory staging blocks and
+//                      one lane issues a TMA tile store (or, for the residual stream, a TMA
+//                      reduce-add), so global writes are whole swizzle rows issued by the copy
+//                      engine and a store drains while the next chunk is packed.
 //
 // Operands are bf16 (kind::f16, K-step 64 per stage) or e4m3 (kind::f8f6f4, K-step 128 per
 // stage); either way a stage row is 128 bytes. K tails and M tails are zero-filled by TMA
@@ -47,8 +48,13 @@ struct GemmShape {
   static constexpr int kBBytes = BN * kStageRowBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiBufBytes = 32 * kEpiChunk * OUT_BYTES;
-  static constexpr int kEpiBytes = EPI_WARPS * kEpiBufBytes;
   static constexpr int kBarrierBytes = 256;
+  // Two staging blocks per warp (a chunk's store drains while the next chunk is packed) unless
+  // that costs the operand ring a stage below four.
+  static constexpr int kFit2 = (kMaxSmem - 1024 - kBarrierBytes - 2 * EPI_WARPS * kEpiBufBytes) / kStageBytes;
+  static constexpr int kFit1 = (kMaxSmem - 1024 - kBarrierBytes - EPI_WARPS * kEpiBufBytes) / kStageBytes;
+  static constexpr int kEpiBuffers = (kFit2 >= 4 || kFit2 == kFit1) ? 2 : 1;
+  static constexpr int kEpiBytes = kEpiBuffers * EPI_WARPS * kEpiBufBytes;
   static constexpr int kFit = (kMaxSmem - 1024 - kBarrierBytes - kEpiBytes) / kStageBytes;
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
   static_assert(kStages >= 2, "not enough shared memory for a 2-stage pipeline");
@@ -60,17 +66,6 @@ __device__ __forceinline__ float rcp_approx(float x) {
   float r;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
   return r;
-}
-
-// Two f32 lanes at once: d = a * b + c (the packed f32 FMA of sm_100).
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{\n\t.reg .b64 pa, pb, pc, pd;\n\t"
-      "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\tmov.b64 pc, {%6, %7};\n\t"
-      "fma.rn.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -397,7 +392,8 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
     constexpr int kParts = kEpiWarps / 4;
     const int quarter = warp & 3;
     const int part = (warp - 2) >> 2;
-    uint8_t* sb = sm_epi + (warp - 2) * kEpiBufBytes;
+    uint8_t* const sb0 = sm_epi + (warp - 2) * S::kEpiBuffers * kEpiBufBytes;
+    int buf = 0;  // staging block of the next chunk
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
@@ -422,8 +418,11 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
         }
         uint4 out[Epi::kOutBytes * 2];
         epi.pack(n0 + c, v, out);
-        // The staging block must no longer be read by this warp's previous store.
-        if (lane == 0) bulk_wait_read<0>();
+        // The staging block must no longer be read by this warp's store from it (the previous
+        // chunk's with one block, the one before with two).
+        uint8_t* sb = sb0 + buf * kEpiBufBytes;
+        buf = buf + 1 == S::kEpiBuffers ? 0 : buf + 1;
+        if (lane == 0) bulk_wait_read<S::kEpiBuffers - 1>();
         __syncwarp();
 #pragma unroll
         for (int j = 0; j < Epi::kOutBytes * 2; ++j)
@@ -481,8 +480,11 @@ struct PairShape {
   static constexpr int kBBytes = kBHalf * kStageRowBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiBufBytes = 32 * kEpiChunk * OUT_BYTES;
-  static constexpr int kEpiBytes = EPI_WARPS * kEpiBufBytes;
   static constexpr int kBarrierBytes = 256;
+  static constexpr int kFit2 = (kMaxSmem - 1024 - kBarrierBytes - 2 * EPI_WARPS * kEpiBufBytes) / kStageBytes;
+  static constexpr int kFit1 = (kMaxSmem - 1024 - kBarrierBytes - EPI_WARPS * kEpiBufBytes) / kStageBytes;
+  static constexpr int kEpiBuffers = (kFit2 >= 4 || kFit2 == kFit1) ? 2 : 1;
+  static constexpr int kEpiBytes = kEpiBuffers * EPI_WARPS * kEpiBufBytes;
   static constexpr int kFit = (kMaxSmem - 1024 - kBarrierBytes - kEpiBytes) / kStageBytes;
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
   static_assert(kStages >= 2, "not enough shared memory for a 2-stage pipeline");
@@ -643,7 +645,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * Epi::kWarp
     constexpr int kParts = kEpiWarps / 4;
     const int quarter = warp & 3;
     const int part = (warp - 2) >> 2;
-    uint8_t* sb = sm_epi + (warp - 2) * kEpiBufBytes;
+    uint8_t* const sb0 = sm_epi + (warp - 2) * S::kEpiBuffers * kEpiBufBytes;
+    int buf = 0;  // staging block of the next chunk
     const uint32_t empty_addr0 = map_to_rank(smem_u32(&tmem_empty[0]), 0);
     const uint32_t empty_addr1 = map_to_rank(smem_u32(&tmem_empty[1]), 0);
     int acc = 0;
@@ -669,7 +672,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * Epi::kWarp
         }
         uint4 out[Epi::kOutBytes * 2];
         epi.pack(n0 + c, v, out);
-        if (lane == 0) bulk_wait_read<0>();
+        uint8_t* sb = sb0 + buf * kEpiBufBytes;
+        buf = buf + 1 == S::kEpiBuffers ? 0 : buf + 1;
+        if (lane == 0) bulk_wait_read<S::kEpiBuffers - 1>();
         __syncwarp();
 #pragma unroll
         for (int j = 0; j < Epi::kOutBytes * 2; ++j)

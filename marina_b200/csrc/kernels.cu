@@ -8,6 +8,7 @@
 #include <type_traits>
 
 #include "kernels.cuh"
+#include "ptx.cuh"
 
 namespace mrn {
 
@@ -240,11 +241,14 @@ constexpr int ln_blocks_per_sm() {
 }
 
 template <int VPL, int VEC>
-__global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel(const __half* __restrict__ x, NormParams n, int rows, int d) {
-  extern __shared__ __align__(16) float gb[];  // gamma [d], beta [d]
+__global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel(const __half* __restrict__ x,
+                                                                                 NormParams n, int rows, int d) {
+  // gamma [d], beta [d], both times the output's 1/scale (1 for bf16 outputs)
+  extern __shared__ __align__(16) float gb[];
+  const float oq = n.out_type == ActType::kE4m3 ? n.inv_q : 1.f;
   for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    gb[i] = n.gamma[i];
-    gb[d + i] = n.beta[i];
+    gb[i] = n.gamma[i] * oq;
+    gb[d + i] = n.beta[i] * oq;
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
@@ -252,6 +256,9 @@ __global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel
   int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
   const size_t out_bytes = n.out_type == ActType::kBf16 ? 2 : 1;
+  // d = 32 VPL; a power of two makes 1/d exact, so the mean is the reference's sum / d
+  constexpr bool kPow2 = (VPL & (VPL - 1)) == 0;
+  const float inv_d = 1.f / static_cast<float>(d);
   using Row = WarpRow<VPL, VEC>;
   using Raw = RawRow<VPL, VEC>;
   Raw r0, r1, r2;
@@ -264,34 +271,35 @@ __global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel
     r0 = r1;
     r1 = r2;
     if (row + 3 * stride < rows) r2.load(x + static_cast<size_t>(row + 3 * stride) * d, lane);
-    float s = 0.f;
+    float2 s2 = make_float2(cur.v[0], cur.v[1]);
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) s += cur.v[i];
-    const float mean = warp_sum(s) / static_cast<float>(d);
-    float q = 0.f;
+    for (int i = 2; i < VPL; i += 2) s2 = add2(s2, make_float2(cur.v[i], cur.v[i + 1]));
+    const float s = warp_sum(s2.x + s2.y);
+    const float mean = kPow2 ? s * inv_d : s / static_cast<float>(d);
+    const float2 nm = make_float2(-mean, -mean);
+    float2 q2 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) q += (cur.v[i] - mean) * (cur.v[i] - mean);
-    const float inv = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(d) + n.eps);
+    for (int i = 0; i < VPL; i += 2) {
+      const float2 c = add2(make_float2(cur.v[i], cur.v[i + 1]), nm);
+      q2 = fma2(c, c, q2);
+    }
+    const float q = warp_sum(q2.x + q2.y);
+    const float inv = rsqrtf((kPow2 ? q * inv_d : q / static_cast<float>(d)) + n.eps);
+    // y = ((v - mean) * inv) * gamma + beta, two lanes per instruction
+    const float2 i2 = make_float2(inv, inv), mi2 = make_float2(-mean * inv, -mean * inv);
 #pragma unroll
     for (int k = 0; k < Row::kChunks; ++k) {
-      // one vector read per chunk: consecutive lanes, consecutive 8 or 16 bytes, no bank conflict
-      float g[VEC], b[VEC];
       const int col = Row::col(k, lane);
-      if constexpr (VEC == 4) {
-        const float4 g4 = *reinterpret_cast<const float4*>(gb + col);
-        const float4 b4 = *reinterpret_cast<const float4*>(gb + d + col);
-        g[0] = g4.x, g[1] = g4.y, g[2] = g4.z, g[3] = g4.w;
-        b[0] = b4.x, b[1] = b4.y, b[2] = b4.z, b[3] = b4.w;
-      } else {
-        const float2 g2 = *reinterpret_cast<const float2*>(gb + col);
-        const float2 b2 = *reinterpret_cast<const float2*>(gb + d + col);
-        g[0] = g2.x, g[1] = g2.y;
-        b[0] = b2.x, b[1] = b2.y;
-      }
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) cur.v[k * VEC + e] = (cur.v[k * VEC + e] - mean) * inv * g[e] + b[e];
+      for (int e = 0; e < VEC; e += 2) {
+        const float2 g = *reinterpret_cast<const float2*>(gb + col + e);
+        const float2 b = *reinterpret_cast<const float2*>(gb + d + col + e);
+        const float2 t = fma2(make_float2(cur.v[k * VEC + e], cur.v[k * VEC + e + 1]), i2, mi2);
+        const float2 y = fma2(t, g, b);
+        cur.v[k * VEC + e] = y.x, cur.v[k * VEC + e + 1] = y.y;
+      }
     }
-    cur.store_act(static_cast<uint8_t*>(n.out) + static_cast<size_t>(row) * d * out_bytes, n.out_type, n.inv_q, lane);
+    cur.store_act(static_cast<uint8_t*>(n.out) + static_cast<size_t>(row) * d * out_bytes, n.out_type, 1.f, lane);
     row += stride;
     if (row >= rows) break;
   }
