@@ -325,7 +325,17 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* 
                : "r"(a));
 }
 
-__device__ __forceinline__ uint32_t lds32(const __nv_bfloat16* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* p) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+
+__device__ __forceinline__ void ldmatrix_x2(uint32_t (&r)[2], const void* p) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(a));
+}
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -415,17 +425,26 @@ __global__ void __launch_bounds__(kAttnWarps * 32, kAttnCtasPerSm) attention_ker
       float s[2 * KS][4];
 #pragma unroll
       for (int nt = 0; nt < 2 * KS; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      // ldmatrix lane roles: lane l supplies the row address of 8x8 matrix l / 8, row l % 8.
+      const int lm = lane >> 3, lr = lane & 7;
 #pragma unroll
       for (int kk = 0; kk < HD; kk += 16) {
+        // A fragment: matrices (rows r0.., k kk), (r0+8.., kk), (r0.., kk+8), (r0+8.., kk+8)
         uint32_t a[4];
-        a[0] = lds32(sq + (r0 + g) * LD + kk + 2 * tq);
-        a[1] = lds32(sq + (r0 + g + 8) * LD + kk + 2 * tq);
-        a[2] = lds32(sq + (r0 + g) * LD + kk + 8 + 2 * tq);
-        a[3] = lds32(sq + (r0 + g + 8) * LD + kk + 8 + 2 * tq);
+        ldmatrix_x4(a, sq + (r0 + (lm & 1) * 8 + lr) * LD + kk + (lm >> 1) * 8);
+        // B fragments of two key tiles per ldmatrix: (keys nt*8.., k kk), (nt*8.., kk+8),
+        // (nt*8+8.., kk), (nt*8+8.., kk+8)
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const __nv_bfloat16* kr = sk + (nt * 8 + g) * LD + kk + 2 * tq;
-          mma_16816(s[nt], a, lds32(kr), lds32(kr + 8));
+        for (int nt = 0; nt + 1 < NT; nt += 2) {
+          uint32_t b[4];
+          ldmatrix_x4(b, sk + (nt * 8 + (lm >> 1) * 8 + lr) * LD + kk + (lm & 1) * 8);
+          mma_16816(s[nt], a, b[0], b[1]);
+          mma_16816(s[nt + 1], a, b[2], b[3]);
+        }
+        if constexpr (NT % 2 == 1) {
+          uint32_t b[2];
+          ldmatrix_x2(b, sk + ((NT - 1) * 8 + lr) * LD + kk + (lm & 1) * 8);
+          mma_16816(s[NT - 1], a, b[0], b[1]);
         }
       }
       // Softmax of rows g (values 0,1) and g+8 (values 2,3); keys >= T are masked.
