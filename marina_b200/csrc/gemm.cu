@@ -44,6 +44,14 @@ cudaError_t launch_pair_epi(const GemmPlan& p, cudaStream_t stream) {
     case Epilogue::kGeluE4m3:
       if constexpr (FP8) return launch_pair<FP8>(p, EpiGelu<true>{a.bias, a.scale, a.inv_q}, stream);
       break;
+    case Epilogue::kGeluTanhBf16:
+      if constexpr (!FP8) return launch_pair<FP8>(p, EpiGeluTanh<false>{a.bias, a.scale, a.inv_q}, stream);
+      break;
+    case Epilogue::kGeluTanhE4m3:
+      if constexpr (FP8) return launch_pair<FP8>(p, EpiGeluTanh<true>{a.bias, a.scale, a.inv_q}, stream);
+      break;
+    default:
+      break;
   }
   return cudaErrorInvalidValue;
 }
@@ -76,6 +84,14 @@ cudaError_t launch_bn(const GemmPlan& p, cudaStream_t stream) {
     case Epilogue::kGeluE4m3:
       if constexpr (FP8) return launch_one<BN, FP8>(p, EpiGelu<true>{a.bias, a.scale, a.inv_q}, stream);
       break;
+    case Epilogue::kGeluTanhBf16:
+      if constexpr (!FP8) return launch_one<BN, FP8>(p, EpiGeluTanh<false>{a.bias, a.scale, a.inv_q}, stream);
+      break;
+    case Epilogue::kGeluTanhE4m3:
+      if constexpr (FP8) return launch_one<BN, FP8>(p, EpiGeluTanh<true>{a.bias, a.scale, a.inv_q}, stream);
+      break;
+    default:
+      break;
   }
   return cudaErrorInvalidValue;
 }
@@ -103,6 +119,8 @@ cudaError_t prepare_bn() {
   if ((e = prepare_one<BN, false, EpiBiasBf16>()) != cudaSuccess) return e;
   if ((e = prepare_one<BN, false, EpiResidual>()) != cudaSuccess) return e;
   if ((e = prepare_one<BN, false, EpiGelu<false>>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, false, EpiGeluTanh<false>>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, true, EpiGeluTanh<true>>()) != cudaSuccess) return e;
   if ((e = prepare_one<BN, true, EpiBiasBf16>()) != cudaSuccess) return e;
   if ((e = prepare_one<BN, true, EpiResidual>()) != cudaSuccess) return e;
   return prepare_one<BN, true, EpiGelu<true>>();
@@ -252,11 +270,11 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
     snprintf(err, 256, "gemm: K=%d rows are not a multiple of 16 bytes", args.k);
     return false;
   }
-  if (args.epi == Epilogue::kGeluE4m3 && !args.fp8) {
+  if ((args.epi == Epilogue::kGeluE4m3 || args.epi == Epilogue::kGeluTanhE4m3) && !args.fp8) {
     snprintf(err, 256, "gemm: e4m3 GELU output is only planned for FP8 operands");
     return false;
   }
-  if (args.epi == Epilogue::kGeluBf16 && args.fp8) {
+  if ((args.epi == Epilogue::kGeluBf16 || args.epi == Epilogue::kGeluTanhBf16) && args.fp8) {
     snprintf(err, 256, "gemm: bf16 GELU output is only planned for bf16 operands");
     return false;
   }
@@ -277,9 +295,11 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
   switch (args.epi) {
     case Epilogue::kBias:
     case Epilogue::kGeluBf16:
+    case Epilogue::kGeluTanhBf16:
       out_ok = make_store_map(&plan->map_out, args.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, args.m, args.n, args.ldo);
       break;
     case Epilogue::kGeluE4m3:
+    case Epilogue::kGeluTanhE4m3:
       out_ok = make_store_map(&plan->map_out, args.out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, args.m, args.n, args.ldo);
       break;
     case Epilogue::kResidual:
@@ -308,6 +328,8 @@ cudaError_t gemm_prepare_device() {
   if ((e = prepare_pair<false, EpiBiasBf16>()) != cudaSuccess) return e;
   if ((e = prepare_pair<false, EpiResidual>()) != cudaSuccess) return e;
   if ((e = prepare_pair<false, EpiGelu<false>>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<false, EpiGeluTanh<false>>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<true, EpiGeluTanh<true>>()) != cudaSuccess) return e;
   if ((e = prepare_pair<true, EpiBiasBf16>()) != cudaSuccess) return e;
   if ((e = prepare_pair<true, EpiResidual>()) != cudaSuccess) return e;
   if ((e = prepare_pair<true, EpiGelu<true>>()) != cudaSuccess) return e;

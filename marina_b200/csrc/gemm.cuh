@@ -222,6 +222,51 @@ struct EpiGelu {
   }
 };
 
+// The tanh-form GELU (Gelu::Tanh, src/net/cpu.rs:270-276 in the reference):
+//     0.5 x (1 + tanh(u)),  u = sqrt(2/pi) (x + 0.044715 x^3),
+// written as relu(x) - |x| s(-2 u(|x|)) with the logistic s(-z) = 1 / (1 + e^z) (since
+// 0.5 (1 + tanh(u)) = s(2u) and u is odd), so the negative tail keeps its relative accuracy
+// where 1 + tanh(u) would cancel. One ex2 and one reciprocal per element; for large |x| the
+// exponential overflows to infinity and the tail term is exactly 0.
+constexpr float kGeluTanhC1 = 0.7978845608028654f * 2.8853900817779268f;  // sqrt(2/pi) * 2 log2(e)
+constexpr float kGeluTanhC3 = kGeluTanhC1 * 0.044715f;
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float a = fabsf(x);
+  const float z = a * fmaf(kGeluTanhC3, a * a, kGeluTanhC1);  // 2 u(|x|) log2(e)
+  const float q = rcp_approx(1.f + ex2_approx(z));
+  return fmaf(-a, q, fmaxf(x, 0.f));
+}
+
+// out = GELU_tanh(acc * scale + bias) as bf16, or as e4m3 codes of value * inv_q.
+template <bool E4M3>
+struct EpiGeluTanh {
+  static constexpr int kOutBytes = E4M3 ? 1 : 2;
+  static constexpr bool kReduce = false;
+  static constexpr int kWarps = 16;
+  const float* bias;
+  float scale;
+  float inv_q;
+  __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[kOutBytes * 2]) const {
+    const float2 s2 = make_float2(scale, scale);
+#pragma unroll
+    for (int c = 0; c < 32; c += 4) {
+      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c));
+      const float2 x0 = fma2(make_float2(v[c], v[c + 1]), s2, make_float2(b.x, b.y));
+      const float2 x1 = fma2(make_float2(v[c + 2], v[c + 3]), s2, make_float2(b.z, b.w));
+      const float y0 = gelu_tanh(x0.x), y1 = gelu_tanh(x0.y), y2 = gelu_tanh(x1.x), y3 = gelu_tanh(x1.y);
+      if constexpr (E4M3) {
+        __nv_fp8x2_storage_t q[2] = {
+            __nv_cvt_float2_to_fp8x2(make_float2(y0 * inv_q, y1 * inv_q), __NV_SATFINITE, __NV_E4M3),
+            __nv_cvt_float2_to_fp8x2(make_float2(y2 * inv_q, y3 * inv_q), __NV_SATFINITE, __NV_E4M3)};
+        reinterpret_cast<uint32_t*>(o)[c / 4] = *reinterpret_cast<const uint32_t*>(q);
+      } else {
+        __nv_bfloat162 p[2] = {__floats2bfloat162_rn(y0, y1), __floats2bfloat162_rn(y2, y3)};
+        reinterpret_cast<uint2*>(o)[c / 4] = *reinterpret_cast<const uint2*>(p);
+      }
+    }
+  }
+};
+
 // x += acc * scale + bias on the f16 residual stream, as a TMA reduce-add of the f16 values.
 struct EpiResidual {
   static constexpr int kOutBytes = 2;

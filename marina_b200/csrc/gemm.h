@@ -14,6 +14,8 @@ enum class Epilogue : int {
   kGeluE4m3 = 2,   // out e4m3 = GELU(acc*scale + bias) * inv_q    (FFN1, FP8 activations)
   kResidual = 3,   // x f16 += acc*scale + bias                    (out-proj, FFN2)
   kResidualLn = 4, // kResidual, then h = LN(x)*gamma + beta       (out-proj -> norm2, FFN2 -> norm1)
+  kGeluTanhBf16 = 5,  // kGeluBf16 with the tanh-form GELU             (FFN1 of Gelu::Tanh cards)
+  kGeluTanhE4m3 = 6,  // kGeluE4m3 with the tanh-form GELU
 };
 
 struct GemmArgs {

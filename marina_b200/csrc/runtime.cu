@@ -270,8 +270,11 @@ void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, b
     g[1].epi = Epilogue::kResidualLn, g[1].gamma = D.n2g, g[1].beta = D.n2b, g[1].ln_out = b.h;
     g[1].ln_inv_q = 1.f / D.as[2];
   }
-  // FFN1: h -> ff = GELU(.)
-  g[2].a = b.h, g[2].b = D.w_1, g[2].n = ff, g[2].k = d, g[2].epi = fp8 ? Epilogue::kGeluE4m3 : Epilogue::kGeluBf16;
+  // FFN1: h -> ff = GELU(.), the card's form (the value head's GELU is always the erf one)
+  const bool tanh_form = c->gelu == MRN_GELU_TANH;
+  g[2].a = b.h, g[2].b = D.w_1, g[2].n = ff, g[2].k = d;
+  g[2].epi = fp8 ? (tanh_form ? Epilogue::kGeluTanhE4m3 : Epilogue::kGeluE4m3)
+                 : (tanh_form ? Epilogue::kGeluTanhBf16 : Epilogue::kGeluBf16);
   g[2].out = b.ff, g[2].ldo = ff, g[2].bias = D.b_1, g[2].scale = scale(2), g[2].inv_q = 1.f / D.as[3];
   // FFN2: ff -> x += (then h = norm1 of the next layer)
   g[3].a = b.ff, g[3].b = D.w_2, g[3].n = d, g[3].k = ff, g[3].epi = Epilogue::kResidual, g[3].out = b.x;
@@ -518,7 +521,8 @@ MRN_API int mrn_create(const mrn_arch* arch, const mrn_weights* weights, int dev
                         c->d, c->dff));
   if (c->t != kTokens)
     return bail(c->fail(MRN_ERR_UNSUPPORTED, "%d tokens per position (the kernels are built for %d)", c->t, kTokens));
-  if (c->gelu != MRN_GELU_ERF) return bail(c->fail(MRN_ERR_UNSUPPORTED, "only the erf GELU is implemented"));
+  if (c->gelu != MRN_GELU_ERF && c->gelu != MRN_GELU_TANH)
+    return bail(c->fail(MRN_ERR_ARGUMENT, "gelu must be MRN_GELU_ERF or MRN_GELU_TANH, got %d", c->gelu));
   if (precision == MRN_PRECISION_FP8) {
     if (!arch->fp8_amax)
       return bail(c->fail(MRN_ERR_ARGUMENT, "FP8 needs the calibration (encoder.fp8.activation_amax); the card has none"));

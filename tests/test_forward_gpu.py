@@ -119,6 +119,28 @@ def test_argmax_agreement_on_1024_positions(net, precision):
     check(compare(priors, wdl, ref_p, ref_w, counts), precision)
 
 
+@pytest.mark.parametrize("precision", ["bf16", "fp8w", "fp8"])
+def test_tanh_gelu_card(precision):
+    """A card trained with the tanh-form GELU ("gelu (tanh approximation)", src/net/model.rs:64-65):
+    the encoder's FFN applies that form, the value head keeps erf (src/net/cpu.rs:130-133)."""
+    import json
+
+    card_json = json.loads(card("nano").to_json())
+    card_json["encoder"]["activation"] = "gelu (tanh approximation)"
+    arch = model.Architecture.from_json(json.dumps(card_json))
+    assert arch.gelu == model.GELU_TANH
+    w = weights.random_init(arch, seed=4)
+    boards, legal, counts, _ = chess.random_positions(43, 128, 0, 80)
+    ref_p, ref_w = oracle.OracleNetwork(arch, weights.fp8_weights(w) if precision != "bf16" else w,
+                                        threads=16).evaluate(boards, legal)
+    priors, wdl = B200Network(arch, w, max_batch=128, precision=precision).evaluate_packed(boards, legal)
+    check(compare(priors, wdl, ref_p, ref_w, counts), precision)
+    # the erf card on the same weights differs, so the form is really applied
+    erf_arch = card("nano")
+    p_erf, _ = B200Network(erf_arch, w, max_batch=128, precision=precision).evaluate_packed(boards, legal)
+    assert float(np.abs(p_erf - priors).max()) > 1e-5
+
+
 def test_biases_and_norm_parameters_are_applied():
     arch = model.nano()
     w = weights.random_init(arch, seed=5, bias_std=0.05, norm_std=0.2)

@@ -13,6 +13,7 @@ from marina_b200 import _lib
 pytestmark = pytest.mark.gpu
 
 EPI_BIAS, EPI_GELU_BF16, EPI_GELU_E4M3, EPI_RESIDUAL = 0, 1, 2, 3
+EPI_GELU_TANH_BF16, EPI_GELU_TANH_E4M3 = 5, 6
 
 # (M, N, K): QKV, out-proj, FFN1, FFN2 of both nets; M = positions x 65.
 SHAPES = [
@@ -82,6 +83,24 @@ def test_gelu_e4m3_epilogue(cuda, m, n, k):
     tol = ref.abs() * 0.0625 + q * 2 ** -6
     ref_sat = ref.clamp(-448 * q, 448 * q)
     assert bool(((got - ref_sat).abs() <= tol + 1e-6).all())
+
+
+@pytest.mark.parametrize("m,n,k", [s for s in SHAPES if s[1] in (768, 2048, 256)])
+def test_gelu_tanh_epilogues(cuda, m, n, k):
+    """The tanh-form GELU (cards trained with it) against torch's approximate="tanh" GELU."""
+    a, b, af, bf, bias = _operands(m, n, k, False, seed=13)
+    out = torch.zeros((m, n), device=cuda, dtype=torch.bfloat16)
+    _run(False, EPI_GELU_TANH_BF16, a, b, bias, out, n, m, n, k)
+    ref = torch.nn.functional.gelu(af @ bf.T + bias, approximate="tanh")
+    assert bool(((out.float() - ref).abs() <= ref.abs() * 2 ** -8 + 1e-5).all())
+    a, b, af, bf, bias = _operands(m, n, k, True, seed=17)
+    scale, q = 0.125, 0.05
+    out8 = torch.zeros((m, n), device=cuda, dtype=torch.uint8)
+    _run(True, EPI_GELU_TANH_E4M3, a, b, bias, out8, n, m, n, k, scale=scale, inv_q=1.0 / q)
+    ref = torch.nn.functional.gelu((af @ bf.T) * scale + bias, approximate="tanh")
+    got = out8.view(torch.float8_e4m3fn).float() * q
+    ref_sat = ref.clamp(-448 * q, 448 * q)
+    assert bool(((got - ref_sat).abs() <= ref.abs() * 0.0625 + q * 2 ** -6 + 1e-6).all())
 
 
 @pytest.mark.parametrize("fp8", [False, True], ids=["bf16", "e4m3"])
