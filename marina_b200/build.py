@@ -27,8 +27,8 @@ INCLUDE = ROOT / "include"
 CUDA_LIB = PKG / "libmarina_b200.so"
 CHESS_LIB = PKG / "libmarina_chess.so"
 
-CUDA_SOURCES = ["gemm.cu", "kernels.cu", "runtime.cu", "static_forward.cu", "api_test.cu"]
-CUDA_HEADERS = ["ptx.cuh", "gemm.cuh", "gemm.h", "tmap.h", "kernels.cuh", "runtime.h"]
+CUDA_SOURCES = ["gemm.cu", "kernels.cu", "attention.cu", "runtime.cu", "static_forward.cu", "api_test.cu"]
+CUDA_HEADERS = ["ptx.cuh", "gemm.cuh", "gemm.h", "gemm_ln.cuh", "tmap.h", "kernels.cuh", "runtime.h"]
 CHESS_SOURCES = ["chess.cpp", "puct.cpp"]
 
 NVCC_FLAGS = [

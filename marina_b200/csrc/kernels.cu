@@ -305,242 +305,6 @@ __global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel
   }
 }
 
-// ---- attention ---------------------------------------------------------------------------
-// Work item = (position, head); Q, K and V of the item (t <= 80 rows, zero-padded to 80) live
-// in shared memory. Warp w owns query rows 16w..16w+15: S = Q K^T for its strip stays in
-// registers (mma.sync m16n8k16, f32 accumulation), the softmax runs on the accumulators with
-// quad shuffles, and the probabilities feed P V straight from registers.
-__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
-  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(a));
-}
-
-__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* p) {
-  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(a));
-}
-
-__device__ __forceinline__ void ldmatrix_x2(uint32_t (&r)[2], const void* p) {
-  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(a));
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
-constexpr int kAttnRows = 80;
-constexpr int kAttnWarps = kAttnRows / 16;
-constexpr int kAttnCtasPerSm = 3;
-
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(a), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-__device__ __forceinline__ float ex2_approx(float x) {
-  float r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
-
-// Persistent: each CTA walks (position, head) items with a stride of the grid, keeping two
-// Q/K/V buffers so the next item's loads (cp.async) overlap the current item's math. Rows
-// T..79 of both buffers are zeroed once and never written again. T (tokens per position) is a
-// template parameter so the key masks fold to constants: key tiles entirely past T are skipped.
-// Each warp writes its normalised 16-row output strip over its own (dead) Q rows in shared
-// memory and stores it with 16-byte writes.
-template <int HD, int T, bool E4M3>
-__global__ void __launch_bounds__(kAttnWarps * 32, kAttnCtasPerSm) attention_kernel(AttentionParams p, int items) {
-  constexpr int LD = HD + 8;  // bf16 elements per staged row (16-byte multiple, conflict-free)
-  constexpr int CH = HD / 8;  // 16-byte chunks per row
-  constexpr int MAT = kAttnRows * LD;
-  constexpr int NT = (T + 7) / 8;    // key tiles of 8 holding at least one valid key
-  constexpr int KS = (T + 15) / 16;  // k16 steps of P V
-  constexpr int ROWS_PER_PASS = kAttnWarps * 32 / CH;
-  static_assert(T <= kAttnRows && 2 * KS <= 10, "tokens per position");
-  extern __shared__ __align__(16) __nv_bfloat16 smem_attn[];  // [2][3][kAttnRows][LD]
-
-  const int d = p.d, heads = p.heads;
-  const __nv_bfloat16* qkv = static_cast<const __nv_bfloat16*>(p.qkv);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, tq = lane & 3;
-  const int r0 = warp * 16;
-
-  for (int i = threadIdx.x; i < 2 * 3 * (kAttnRows - T) * CH; i += blockDim.x) {
-    const int per_mat = (kAttnRows - T) * CH;
-    const int m = i / per_mat, rem = i - m * per_mat;
-    const int row = T + rem / CH, ch = rem % CH;
-    *reinterpret_cast<uint4*>(smem_attn + m * MAT + row * LD + ch * 8) = make_uint4(0, 0, 0, 0);
-  }
-
-  const int ld_ch = threadIdx.x % CH, ld_row0 = threadIdx.x / CH;
-  auto load = [&](int item, int buf) {
-    const int pos = item / heads, head = item - pos * heads;
-    const __nv_bfloat16* base = qkv + static_cast<size_t>(pos) * T * 3 * d + head * HD + ld_ch * 8;
-    __nv_bfloat16* dst = smem_attn + buf * 3 * MAT + ld_ch * 8;
-#pragma unroll
-    for (int m = 0; m < 3; ++m)
-#pragma unroll
-      for (int row = ld_row0; row < T; row += ROWS_PER_PASS)
-        cp_async16(dst + m * MAT + row * LD, base + static_cast<size_t>(row) * 3 * d + m * d);
-  };
-
-  int item = blockIdx.x;
-  if (item < items) load(item, 0);
-  cp_async_commit();
-  const float scale_log2 = rsqrtf(static_cast<float>(HD)) * 1.4426950408889634f;
-  for (int it = 0; item < items; ++it, item += gridDim.x) {
-    const int buf = it & 1;
-    const int next = item + gridDim.x;
-    if (next < items) load(next, buf ^ 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-
-    __nv_bfloat16* sq = smem_attn + buf * 3 * MAT;
-    const __nv_bfloat16* sk = sq + MAT;
-    const __nv_bfloat16* sv = sk + MAT;
-    const int pos = item / heads, head = item - pos * heads;
-    if (r0 < T) {
-      // S = Q K^T for rows r0..r0+15 against the key tiles holding valid keys.
-      float s[2 * KS][4];
-#pragma unroll
-      for (int nt = 0; nt < 2 * KS; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-      // ldmatrix lane roles: lane l supplies the row address of 8x8 matrix l / 8, row l % 8.
-      const int lm = lane >> 3, lr = lane & 7;
-#pragma unroll
-      for (int kk = 0; kk < HD; kk += 16) {
-        // A fragment: matrices (rows r0.., k kk), (r0+8.., kk), (r0.., kk+8), (r0+8.., kk+8)
-        uint32_t a[4];
-        ldmatrix_x4(a, sq + (r0 + (lm & 1) * 8 + lr) * LD + kk + (lm >> 1) * 8);
-        // B fragments of two key tiles per ldmatrix: (keys nt*8.., k kk), (nt*8.., kk+8),
-        // (nt*8+8.., kk), (nt*8+8.., kk+8)
-#pragma unroll
-        for (int nt = 0; nt + 1 < NT; nt += 2) {
-          uint32_t b[4];
-          ldmatrix_x4(b, sk + (nt * 8 + (lm >> 1) * 8 + lr) * LD + kk + (lm & 1) * 8);
-          mma_16816(s[nt], a, b[0], b[1]);
-          mma_16816(s[nt + 1], a, b[2], b[3]);
-        }
-        if constexpr (NT % 2 == 1) {
-          uint32_t b[2];
-          ldmatrix_x2(b, sk + ((NT - 1) * 8 + lr) * LD + kk + (lm & 1) * 8);
-          mma_16816(s[NT - 1], a, b[0], b[1]);
-        }
-      }
-      // Softmax of rows g (values 0,1) and g+8 (values 2,3); keys >= T are masked.
-      float m0 = -INFINITY, m1 = -INFINITY;
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-          if (nt * 8 + 7 < T || nt * 8 + 2 * tq + j < T) {
-            m0 = fmaxf(m0, s[nt][j]);
-            m1 = fmaxf(m1, s[nt][2 + j]);
-          }
-      m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
-      m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
-      m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
-      m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
-      const float b0 = -m0 * scale_log2, b1 = -m1 * scale_log2;
-      float l0 = 0.f, l1 = 0.f;
-#pragma unroll
-      for (int nt = 0; nt < 2 * KS; ++nt)
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          if (nt >= NT) {
-            s[nt][j] = s[nt][2 + j] = 0.f;
-          } else if (nt * 8 + 7 < T || nt * 8 + 2 * tq + j < T) {
-            s[nt][j] = ex2_approx(fmaf(s[nt][j], scale_log2, b0));
-            s[nt][2 + j] = ex2_approx(fmaf(s[nt][2 + j], scale_log2, b1));
-          } else {
-            s[nt][j] = s[nt][2 + j] = 0.f;
-          }
-          l0 += s[nt][j];
-          l1 += s[nt][2 + j];
-        }
-      l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-      l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-      l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-      l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-
-      // O = P V: P comes from the S accumulators (two n-tiles make one k16 A fragment).
-      float o[HD / 8][4];
-#pragma unroll
-      for (int nt = 0; nt < HD / 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < KS; ++kk) {
-        uint32_t a[4];
-        a[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-        a[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-        a[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-        a[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-        const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-#pragma unroll
-        for (int nt = 0; nt < HD / 8; nt += 2) {
-          uint32_t b[4];
-          ldmatrix_x4_trans(b, sv + key * LD + nt * 8 + ((lane >> 4) & 1) * 8);
-          mma_16816(o[nt], a, b[0], b[1]);
-          mma_16816(o[nt + 1], a, b[2], b[3]);
-        }
-      }
-
-      // Normalised strip -> this warp's Q rows (no longer read) -> 16-byte global stores.
-      const float inv0 = 1.f / l0, inv1 = 1.f / l1;
-      __syncwarp();
-#pragma unroll
-      for (int nt = 0; nt < HD / 8; ++nt) {
-        const int col = nt * 8 + 2 * tq;
-        if constexpr (E4M3) {
-          uint8_t* so = reinterpret_cast<uint8_t*>(sq);
-          *reinterpret_cast<__nv_fp8x2_storage_t*>(so + (r0 + g) * (LD * 2) + col) = __nv_cvt_float2_to_fp8x2(
-              make_float2(o[nt][0] * inv0 * p.inv_q, o[nt][1] * inv0 * p.inv_q), __NV_SATFINITE, __NV_E4M3);
-          *reinterpret_cast<__nv_fp8x2_storage_t*>(so + (r0 + g + 8) * (LD * 2) + col) = __nv_cvt_float2_to_fp8x2(
-              make_float2(o[nt][2] * inv1 * p.inv_q, o[nt][3] * inv1 * p.inv_q), __NV_SATFINITE, __NV_E4M3);
-        } else {
-          *reinterpret_cast<__nv_bfloat162*>(sq + (r0 + g) * LD + col) = __floats2bfloat162_rn(o[nt][0] * inv0, o[nt][1] * inv0);
-          *reinterpret_cast<__nv_bfloat162*>(sq + (r0 + g + 8) * LD + col) =
-              __floats2bfloat162_rn(o[nt][2] * inv1, o[nt][3] * inv1);
-        }
-      }
-      __syncwarp();
-      constexpr int kRowBytes = HD * (E4M3 ? 1 : 2);
-      constexpr int kChunks = kRowBytes / 16;  // 16-byte chunks per output row
-      for (int i = lane; i < 16 * kChunks; i += 32) {
-        const int rr = i / kChunks, c = i - rr * kChunks;
-        const int row = r0 + rr;
-        if (row >= T) continue;
-        const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(sq) + row * (LD * 2) + c * 16);
-        uint8_t* dst = static_cast<uint8_t*>(p.out) +
-                       ((static_cast<size_t>(pos) * T + row) * d + head * HD) * (E4M3 ? 1 : 2) + c * 16;
-        *reinterpret_cast<uint4*>(dst) = v;
-      }
-    }
-    // Every warp is done with `buf` before the load two items ahead overwrites it.
-    __syncthreads();
-  }
-  cp_async_wait<0>();
-}
-
 // ---- heads -----------------------------------------------------------------------------
 // One CTA (8 warps) per position. Each warp takes legal slots in turn: the slot's square token
 // gets the final norm and the policy norm in registers (src/net/cpu.rs:137,140-152) and its
@@ -722,45 +486,6 @@ cudaError_t launch_embed_ln(const EmbedParams& e, const NormParams& n, int posit
 
 cudaError_t launch_layernorm(const __half* x, const NormParams& n, int rows, int d, cudaStream_t s) {
   return dispatch_d<NormLaunch>(d, x, n, rows, s);
-}
-
-namespace {
-template <int HD, int T>
-cudaError_t launch_attention_t(const AttentionParams& p, int grid, int items, cudaStream_t s) {
-  const size_t smem = 2 * 3 * kAttnRows * (HD + 8) * sizeof(__nv_bfloat16);
-  if (p.out_type == ActType::kE4m3)
-    attention_kernel<HD, T, true><<<grid, kAttnWarps * 32, smem, s>>>(p, items);
-  else
-    attention_kernel<HD, T, false><<<grid, kAttnWarps * 32, smem, s>>>(p, items);
-  return cudaGetLastError();
-}
-
-template <int HD, int T>
-cudaError_t prepare_attention_t() {
-  const int smem = 2 * 3 * kAttnRows * (HD + 8) * 2;
-  cudaError_t e = cudaFuncSetAttribute(attention_kernel<HD, T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(attention_kernel<HD, T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-}
-}  // namespace
-
-// Board mode has 65 tokens (one state token, 64 squares; src/net/model.rs:17).
-cudaError_t launch_attention(const AttentionParams& p, int positions, int head_dim, cudaStream_t s) {
-  if (p.t != 65) return cudaErrorInvalidValue;
-  int dev = 0, sms = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int items = positions * p.heads;
-  const int grid = items < sms * kAttnCtasPerSm ? items : sms * kAttnCtasPerSm;
-  if (head_dim == 64) return launch_attention_t<64, 65>(p, grid, items, s);
-  if (head_dim == 32) return launch_attention_t<32, 65>(p, grid, items, s);
-  return cudaErrorInvalidValue;
-}
-
-cudaError_t prepare_attention() {
-  cudaError_t e = prepare_attention_t<64, 65>();
-  if (e != cudaSuccess) return e;
-  return prepare_attention_t<32, 65>();
 }
 
 cudaError_t launch_heads(const HeadsParams& p, int positions, int d, cudaStream_t s) {

@@ -45,7 +45,9 @@ struct AttentionParams {
   ActType out_type;
   float inv_q;
   int t, d, heads;
+  int* status;       // device error word (a bounded wait that gave up), may be null
 };
+// attention.cu: per (position, head) softmax attention; builds the qkv tensor map on each call.
 cudaError_t launch_attention(const AttentionParams& p, int positions, int head_dim, cudaStream_t s);
 // Opt the attention kernels into their dynamic shared memory (once per device).
 cudaError_t prepare_attention();

@@ -357,7 +357,7 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
     CK(mrn::gemm_launch(plans[0], s));
     done();
     mark(MRN_PROFILE_ATTENTION);
-    CK(mrn::launch_attention(mrn::AttentionParams{c->qkv, c->attn, act, 1.f / D.as[1], c->t, d, c->heads}, P,
+    CK(mrn::launch_attention(mrn::AttentionParams{c->qkv, c->attn, act, 1.f / D.as[1], c->t, d, c->heads, c->status}, P,
                              d / c->heads, s));
     done();
     mark(MRN_PROFILE_GEMM);

@@ -150,7 +150,7 @@ int forward(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, floa
     mrn::GemmArgs g[4];
     mrn::layer_gemm_args(c, l, R, bufs, fuse, g);
     if ((rc = gemm(c, g[0], s))) return rc;
-    CKS(mrn::launch_attention(mrn::AttentionParams{qkv, attn, act, 1.f / D.as[1], c->t, d, c->heads}, n,
+    CKS(mrn::launch_attention(mrn::AttentionParams{qkv, attn, act, 1.f / D.as[1], c->t, d, c->heads, c->status}, n,
                               d / c->heads, s));
     if ((rc = residual(c, l, 0, g[1], bufs, s))) return rc;
     if ((rc = gemm(c, g[2], s))) return rc;
