@@ -32,6 +32,11 @@ sys.path.insert(0, str(ROOT))
 if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
     os.environ["NCCL_DEBUG"] = "WARN"
 
+# DRAM bytes (read + write) of all GEMM launches of one forward pass, per position: ncu
+# dram__bytes_read.sum + dram__bytes_write.sum summed over the 49 GEMM launches of one pass of
+# `bench.py --batch 1024 --precision fp8` (the traffic grows with the rows; the weights are
+# 19 MB a pass). Traffic of one full pass = this x the batch.
+GEMM_DRAM_BYTES_PER_EVAL = {("small", "fp8"): 7.60e6}
 METRIC = "small-net evals/sec per B200 and 8xB200 at batch 256-8192; PUCT nodes/sec"
 UNIT = "evals/s"
 L2_BYTES = 126 * 2 ** 20
@@ -48,9 +53,10 @@ def parse_args():
     ap.add_argument("--precision", choices=["fp8", "fp8w", "bf16"], default="fp8")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["step", "sweep", "puct", "wholebox"], default="step",
+    ap.add_argument("--mode", choices=["step", "sweep", "puct", "wholebox", "gemm"], default="step",
                     help="step: the contract's JSON line; sweep: configs[2] latency/throughput per batch size; "
-                         "puct: configs[3] nodes/s of the batched PUCT search; wholebox: configs[4] 1M positions")
+                         "puct: configs[3] nodes/s of the batched PUCT search; wholebox: configs[4] 1M positions; "
+                         "gemm: the four encoder GEMMs of the batch beside cuBLASLt (torch._scaled_mm) on the same shapes")
     ap.add_argument("--roots", type=int, default=32)
     ap.add_argument("--nodes", type=int, default=100_000)
     ap.add_argument("--positions", type=int, default=1 << 20)
@@ -309,6 +315,8 @@ def run_ours(args):
             else (1400.0, "fallback bf16 sustained")
     g = prof["gemm"]
     achieved = g["flops"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else 0.0
+    traffic = GEMM_DRAM_BYTES_PER_EVAL.get((args.net, args.precision))
+    traffic = traffic * B if traffic else None
     total_prof_ms = sum(v["ms"] for v in prof.values())
 
     launches = net.launches_per_forward(B) * args.steps
@@ -321,7 +329,8 @@ def run_ours(args):
             "data": "synthetic (seeded random-playout positions; random-init weights)",
             "config": workload_config(args, world),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None, "kernel": "gemm_tc_kernel (all GEMM launches of one pass)",
+                         "frac": achieved / peak, "traffic": traffic, "traffic_unit": "bytes per pass (DRAM, all GEMM launches)",
+                         "kernel": "gemm_tc_kernel (all GEMM launches of one pass)",
                          "peak_source": peak_src, "flops_per_eval": flops_per_eval(arch)},
             "kernel_ms": {k: round(v["ms"], 4) for k, v in prof.items()},
             "kernel_share": {k: round(v["ms"] / total_prof_ms, 4) for k, v in prof.items()} if total_prof_ms else {},
@@ -464,6 +473,61 @@ def run_wholebox(args):
         net.close()
 
 
+def run_gemm(args):
+    """Our tcgen05 GEMM (through mrn_test_gemm) and cuBLASLt FP8 (torch._scaled_mm, e4m3 x e4m3 ->
+    bf16 with a bias) on the encoder's four GEMM shapes at this batch, e4m3 operands. cuBLASLt gets
+    the plain bias epilogue on every shape (its residual would be a bf16 beta=1 add); ours runs the
+    epilogue the forward pass uses (bias->bf16, GELU->e4m3, f16 residual add). CUDA events, after
+    warm-up; inputs > L2."""
+    import ctypes
+
+    import torch
+
+    from marina_b200 import _lib
+
+    arch, _ = load_net(args.net)
+    d, ff, M = arch.d_model, arch.d_ff, args.batch * 65
+    dev = torch.device("cuda", 0)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = []
+    for name, N, K, epi, odt in [("qkv", 3 * d, d, 0, torch.bfloat16), ("out_proj", d, d, 3, torch.float16),
+                                 ("ffn1", ff, d, 2, torch.uint8), ("ffn2", d, ff, 3, torch.float16)]:
+        a = (torch.randn(M, K, device=dev) * 0.5).to(torch.float8_e4m3fn)
+        b = (torch.randn(N, K, device=dev) * 0.5).to(torch.float8_e4m3fn)
+        bias = torch.randn(N, device=dev)
+        o = torch.zeros(M, N, device=dev, dtype=odt)
+
+        def ours():
+            rc = lib.mrn_test_gemm(1, epi, a.data_ptr(), b.data_ptr(), bias.data_ptr(), o.data_ptr(), N, M, N, K,
+                                   1e-3, 10.0, ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(stream))
+            assert rc == 0, lib.mrn_test_last_error().decode()
+
+        one, bias16 = torch.tensor(1.0, device=dev), bias.to(torch.bfloat16)
+
+        def cublas():
+            torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, bias=bias16, out_dtype=torch.bfloat16)
+
+        row = {"gemm": name, "M": M, "N": N, "K": K}
+        for label, fn in (("ours_us", ours), ("cublaslt_us", cublas)):
+            for _ in range(max(3, args.warmup)):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            row[label] = e0.elapsed_time(e1) / args.steps * 1e3
+        row["ours_tflops"] = 2 * M * N * K / row["ours_us"] / 1e6
+        row["cublaslt_tflops"] = 2 * M * N * K / row["cublaslt_us"] / 1e6
+        assert int(status.item()) == 0
+        out.append(row)
+    print(json.dumps({"mode": "gemm", "net": args.net, "batch": args.batch, "dtype": "e4m3", "shapes": out}), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
@@ -474,6 +538,8 @@ def main():
         run_puct(args)
     elif args.mode == "wholebox":
         run_wholebox(args)
+    elif args.mode == "gemm":
+        run_gemm(args)
     else:
         run_ours(args)
 

@@ -285,18 +285,24 @@ __global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel
     }
     const float q = warp_sum(q2.x + q2.y);
     const float inv = rsqrtf((kPow2 ? q * inv_d : q / static_cast<float>(d)) + n.eps);
-    // y = ((v - mean) * inv) * gamma + beta, two lanes per instruction
+    // y = ((v - mean) * inv) * gamma + beta, two lanes per instruction, gamma/beta as 16-byte reads
     const float2 i2 = make_float2(inv, inv), mi2 = make_float2(-mean * inv, -mean * inv);
 #pragma unroll
     for (int k = 0; k < Row::kChunks; ++k) {
       const int col = Row::col(k, lane);
-#pragma unroll
-      for (int e = 0; e < VEC; e += 2) {
-        const float2 g = *reinterpret_cast<const float2*>(gb + col + e);
-        const float2 b = *reinterpret_cast<const float2*>(gb + d + col + e);
-        const float2 t = fma2(make_float2(cur.v[k * VEC + e], cur.v[k * VEC + e + 1]), i2, mi2);
-        const float2 y = fma2(t, g, b);
-        cur.v[k * VEC + e] = y.x, cur.v[k * VEC + e + 1] = y.y;
+      if constexpr (VEC == 4) {
+        const float4 g = *reinterpret_cast<const float4*>(gb + col);
+        const float4 b = *reinterpret_cast<const float4*>(gb + d + col);
+        const float2 t0 = fma2(make_float2(cur.v[k * 4], cur.v[k * 4 + 1]), i2, mi2);
+        const float2 t1 = fma2(make_float2(cur.v[k * 4 + 2], cur.v[k * 4 + 3]), i2, mi2);
+        const float2 y0 = fma2(t0, make_float2(g.x, g.y), make_float2(b.x, b.y));
+        const float2 y1 = fma2(t1, make_float2(g.z, g.w), make_float2(b.z, b.w));
+        cur.v[k * 4] = y0.x, cur.v[k * 4 + 1] = y0.y, cur.v[k * 4 + 2] = y1.x, cur.v[k * 4 + 3] = y1.y;
+      } else {
+        const float2 g = *reinterpret_cast<const float2*>(gb + col);
+        const float2 b = *reinterpret_cast<const float2*>(gb + d + col);
+        const float2 y = fma2(fma2(make_float2(cur.v[k * 2], cur.v[k * 2 + 1]), i2, mi2), g, b);
+        cur.v[k * 2] = y.x, cur.v[k * 2 + 1] = y.y;
       }
     }
     cur.store_act(static_cast<uint8_t*>(n.out) + static_cast<size_t>(row) * d * out_bytes, n.out_type, 1.f, lane);
