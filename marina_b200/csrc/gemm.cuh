@@ -97,7 +97,7 @@ __device__ __forceinline__ __half2 f32x2_to_h2_sat(float2 v) {
 // least-squares fits on Chebyshev nodes made by gelu_fit.py beside this file; a is clamped
 // at the fit's bound, past which Phi(-a) no longer moves the output by half an ulp.
 //   f32 form (bf16 outputs): degree 7, |relative GELU error| <= 4.3e-6.
-//   packed f16 form (outputs rounded to e4m3 next, 12.5% steps): degree 5, <= 1.1e-2,
+//   packed f16 form (outputs rounded to e4m3 next, 12.5% steps): degree 4, <= 1.0e-2,
 //   most of it the f16 rounding of x itself.
 // kGeluF32: degree 7 on [0, 5.5], max relative GELU error 4.21e-06 in float32
 constexpr float kGeluF32Bound = 5.5f;
@@ -109,14 +109,13 @@ constexpr float kGeluF32_4 = 8.556272268e-03f;
 constexpr float kGeluF32_5 = -9.434208502e-04f;
 constexpr float kGeluF32_6 = 6.328849712e-05f;
 constexpr float kGeluF32_7 = -1.921234625e-06f;
-// kGeluF16: degree 5 on [0, 5.0], max relative GELU error 1.11e-02 in float16
-constexpr float kGeluF16Bound = 5.0f;
-constexpr float kGeluF16_0 = -1.000238752e+00f;
-constexpr float kGeluF16_1 = -1.147657292e+00f;
-constexpr float kGeluF16_2 = -4.671405841e-01f;
-constexpr float kGeluF16_3 = -4.618088635e-02f;
-constexpr float kGeluF16_4 = 5.264457609e-03f;
-constexpr float kGeluF16_5 = -2.672135067e-04f;
+// kGeluF16: degree 4 on [0, 4.5], max relative GELU error 1.00e-02 in float16
+constexpr float kGeluF16Bound = 4.5f;
+constexpr float kGeluF16_0 = -1.001255186e+00f;
+constexpr float kGeluF16_1 = -1.136516071e+00f;
+constexpr float kGeluF16_2 = -4.867097285e-01f;
+constexpr float kGeluF16_3 = -3.413367701e-02f;
+constexpr float kGeluF16_4 = 2.233444850e-03f;
 
 // GELU of two f32 values, packed arithmetic for the polynomial.
 __device__ __forceinline__ float2 gelu2(float2 x) {
@@ -137,8 +136,7 @@ __device__ __forceinline__ float2 gelu2(float2 x) {
 __device__ __forceinline__ __half2 gelu_h2(__half2 x) {
   const __half2 a = __habs2(x);
   const __half2 t = __hmin2(a, __float2half2_rn(kGeluF16Bound));
-  __half2 p = __hfma2(t, __float2half2_rn(kGeluF16_5), __float2half2_rn(kGeluF16_4));
-  p = __hfma2(t, p, __float2half2_rn(kGeluF16_3));
+  __half2 p = __hfma2(t, __float2half2_rn(kGeluF16_4), __float2half2_rn(kGeluF16_3));
   p = __hfma2(t, p, __float2half2_rn(kGeluF16_2));
   p = __hfma2(t, p, __float2half2_rn(kGeluF16_1));
   p = __hfma2(t, p, __float2half2_rn(kGeluF16_0));
