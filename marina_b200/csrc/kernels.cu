@@ -96,41 +96,6 @@ struct WarpRow {
     }
   }
 
-  // In place: LayerNorm over the d values (biased variance, two passes, as PyTorch).
-  __device__ __forceinline__ void layernorm(const float* __restrict__ g, const float* __restrict__ b, float eps,
-                                            int d, int lane) {
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) s += v[i];
-    const float mean = warp_sum(s) / static_cast<float>(d);
-    float q = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) q += (v[i] - mean) * (v[i] - mean);
-    const float inv = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(d) + eps);
-#pragma unroll
-    for (int c = 0; c < kChunks; ++c) {
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        const int k = col(c, lane) + e;
-        v[c * VEC + e] = (v[c * VEC + e] - mean) * inv * __ldg(g + k) + __ldg(b + k);
-      }
-    }
-  }
-
-  // The same with gamma and beta already in registers (same element layout as this row).
-  __device__ __forceinline__ void layernorm_regs(const WarpRow& g, const WarpRow& b, float eps, int d) {
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) s += v[i];
-    const float mean = warp_sum(s) / static_cast<float>(d);
-    float q = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) q += (v[i] - mean) * (v[i] - mean);
-    const float inv = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(d) + eps);
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) v[i] = (v[i] - mean) * inv * g.v[i] + b.v[i];
-  }
-
   __device__ __forceinline__ void store_act(void* dst, ActType type, float inv_q, int lane) const {
 #pragma unroll
     for (int c = 0; c < kChunks; ++c) {
@@ -159,9 +124,69 @@ struct WarpRow {
   }
 };
 
+// ---- LayerNorm arithmetic shared by the embedding and LayerNorm kernels -------------------
+// (mean, 1/sqrt(var + eps)) of a warp-held row: biased two-pass variance as src/net/cpu.rs:331-336,
+// on packed f32x2 arithmetic; d = 32 VPL, and a power-of-two d makes 1/d exact, so the mean is the
+// reference's sum / d.
+template <int VPL, int VEC>
+__device__ __forceinline__ float2 ln_stats(const WarpRow<VPL, VEC>& cur, int d, float eps) {
+  constexpr bool kPow2 = (VPL & (VPL - 1)) == 0;
+  const float inv_d = 1.f / static_cast<float>(d);
+  float2 s2 = make_float2(cur.v[0], cur.v[1]);
+#pragma unroll
+  for (int i = 2; i < VPL; i += 2) s2 = add2(s2, make_float2(cur.v[i], cur.v[i + 1]));
+  const float s = warp_sum(s2.x + s2.y);
+  const float mean = kPow2 ? s * inv_d : s / static_cast<float>(d);
+  const float2 nm = make_float2(-mean, -mean);
+  float2 q2 = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < VPL; i += 2) {
+    const float2 c = add2(make_float2(cur.v[i], cur.v[i + 1]), nm);
+    q2 = fma2(c, c, q2);
+  }
+  const float q = warp_sum(q2.x + q2.y);
+  return make_float2(mean, rsqrtf((kPow2 ? q * inv_d : q / static_cast<float>(d)) + eps));
+}
+
+// In place: y = ((v - mean) * inv) * gamma + beta, gamma/beta read as vectors from `g`/`b`
+// (shared or global memory, element k of the row at g[k]).
+template <int VPL, int VEC>
+__device__ __forceinline__ void ln_apply(WarpRow<VPL, VEC>& cur, const float* g, const float* b, float2 stats,
+                                         int lane) {
+  using Row = WarpRow<VPL, VEC>;
+  const float inv = stats.y, mean = stats.x;
+  const float2 i2 = make_float2(inv, inv), mi2 = make_float2(-mean * inv, -mean * inv);
+#pragma unroll
+  for (int k = 0; k < Row::kChunks; ++k) {
+    const int col = Row::col(k, lane);
+    if constexpr (VEC == 4) {
+      const float4 g4 = *reinterpret_cast<const float4*>(g + col);
+      const float4 b4 = *reinterpret_cast<const float4*>(b + col);
+      const float2 t0 = fma2(make_float2(cur.v[k * 4], cur.v[k * 4 + 1]), i2, mi2);
+      const float2 t1 = fma2(make_float2(cur.v[k * 4 + 2], cur.v[k * 4 + 3]), i2, mi2);
+      const float2 y0 = fma2(t0, make_float2(g4.x, g4.y), make_float2(b4.x, b4.y));
+      const float2 y1 = fma2(t1, make_float2(g4.z, g4.w), make_float2(b4.z, b4.w));
+      cur.v[k * 4] = y0.x, cur.v[k * 4 + 1] = y0.y, cur.v[k * 4 + 2] = y1.x, cur.v[k * 4 + 3] = y1.y;
+    } else {
+      const float2 g2 = *reinterpret_cast<const float2*>(g + col);
+      const float2 b2 = *reinterpret_cast<const float2*>(b + col);
+      const float2 y = fma2(fma2(make_float2(cur.v[k * 2], cur.v[k * 2 + 1]), i2, mi2), g2, b2);
+      cur.v[k * 2] = y.x, cur.v[k * 2 + 1] = y.y;
+    }
+  }
+}
+
 // ---- embedding + layer 0 norm1 (src/net/cpu.rs:59-84, src/net/cuda/kernels.cu:69-100) ----
 template <int VPL, int VEC>
 __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedParams e, NormParams n, int rows, int d) {
+  // gamma [d], beta [d], both times the output's 1/scale (1 for bf16 outputs)
+  extern __shared__ __align__(16) float gb[];
+  const float oq = n.out_type == ActType::kE4m3 ? n.inv_q : 1.f;
+  for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    gb[k] = n.gamma[k] * oq;
+    gb[d + k] = n.beta[k] * oq;
+  }
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -187,14 +212,11 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedParams e, NormParams
   } else if (i >= e.square_start && i < e.square_start + 64) {
     const int s = i - e.square_start;
     const int piece = b[s] < 13 ? b[s] : 0;
+    Row sq;
+    r.load(e.piece_embed + static_cast<size_t>(piece) * d, lane);
+    sq.load(e.square_embed + static_cast<size_t>(s) * d, lane);
 #pragma unroll
-    for (int c = 0; c < Row::kChunks; ++c)
-#pragma unroll
-      for (int k = 0; k < VEC; ++k) {
-        const int o = Row::col(c, lane) + k;
-        r.v[c * VEC + k] =
-            __ldg(e.piece_embed + static_cast<size_t>(piece) * d + o) + __ldg(e.square_embed + static_cast<size_t>(s) * d + o);
-      }
+    for (int k = 0; k < VPL; ++k) r.v[k] += sq.v[k];
   } else {
 #pragma unroll
     for (int k = 0; k < VPL; ++k) r.v[k] = 0.f;
@@ -202,9 +224,9 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedParams e, NormParams
   // norm1 sees the f16 values the residual stream keeps
   r.round_to_half();
   r.store(e.x + static_cast<size_t>(row) * d, lane);
-  r.layernorm(n.gamma, n.beta, n.eps, d, lane);
+  ln_apply(r, gb, gb + d, ln_stats(r, d, n.eps), lane);
   const size_t off = static_cast<size_t>(row) * d * (n.out_type == ActType::kBf16 ? 2 : 1);
-  r.store_act(static_cast<uint8_t*>(n.out) + off, n.out_type, n.inv_q, lane);
+  r.store_act(static_cast<uint8_t*>(n.out) + off, n.out_type, 1.f, lane);
 }
 
 // ---- LayerNorm, one warp per row (src/net/cpu.rs:323-343) --------------------------------
@@ -256,9 +278,6 @@ __global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel
   int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
   const size_t out_bytes = n.out_type == ActType::kBf16 ? 2 : 1;
-  // d = 32 VPL; a power of two makes 1/d exact, so the mean is the reference's sum / d
-  constexpr bool kPow2 = (VPL & (VPL - 1)) == 0;
-  const float inv_d = 1.f / static_cast<float>(d);
   using Row = WarpRow<VPL, VEC>;
   using Raw = RawRow<VPL, VEC>;
   Raw r0, r1, r2;
@@ -271,40 +290,7 @@ __global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel
     r0 = r1;
     r1 = r2;
     if (row + 3 * stride < rows) r2.load(x + static_cast<size_t>(row + 3 * stride) * d, lane);
-    float2 s2 = make_float2(cur.v[0], cur.v[1]);
-#pragma unroll
-    for (int i = 2; i < VPL; i += 2) s2 = add2(s2, make_float2(cur.v[i], cur.v[i + 1]));
-    const float s = warp_sum(s2.x + s2.y);
-    const float mean = kPow2 ? s * inv_d : s / static_cast<float>(d);
-    const float2 nm = make_float2(-mean, -mean);
-    float2 q2 = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int i = 0; i < VPL; i += 2) {
-      const float2 c = add2(make_float2(cur.v[i], cur.v[i + 1]), nm);
-      q2 = fma2(c, c, q2);
-    }
-    const float q = warp_sum(q2.x + q2.y);
-    const float inv = rsqrtf((kPow2 ? q * inv_d : q / static_cast<float>(d)) + n.eps);
-    // y = ((v - mean) * inv) * gamma + beta, two lanes per instruction, gamma/beta as 16-byte reads
-    const float2 i2 = make_float2(inv, inv), mi2 = make_float2(-mean * inv, -mean * inv);
-#pragma unroll
-    for (int k = 0; k < Row::kChunks; ++k) {
-      const int col = Row::col(k, lane);
-      if constexpr (VEC == 4) {
-        const float4 g = *reinterpret_cast<const float4*>(gb + col);
-        const float4 b = *reinterpret_cast<const float4*>(gb + d + col);
-        const float2 t0 = fma2(make_float2(cur.v[k * 4], cur.v[k * 4 + 1]), i2, mi2);
-        const float2 t1 = fma2(make_float2(cur.v[k * 4 + 2], cur.v[k * 4 + 3]), i2, mi2);
-        const float2 y0 = fma2(t0, make_float2(g.x, g.y), make_float2(b.x, b.y));
-        const float2 y1 = fma2(t1, make_float2(g.z, g.w), make_float2(b.z, b.w));
-        cur.v[k * 4] = y0.x, cur.v[k * 4 + 1] = y0.y, cur.v[k * 4 + 2] = y1.x, cur.v[k * 4 + 3] = y1.y;
-      } else {
-        const float2 g = *reinterpret_cast<const float2*>(gb + col);
-        const float2 b = *reinterpret_cast<const float2*>(gb + d + col);
-        const float2 y = fma2(fma2(make_float2(cur.v[k * 2], cur.v[k * 2 + 1]), i2, mi2), g, b);
-        cur.v[k * 2] = y.x, cur.v[k * 2 + 1] = y.y;
-      }
-    }
+    ln_apply(cur, gb, gb + d, ln_stats(cur, d, n.eps), lane);
     cur.store_act(static_cast<uint8_t*>(n.out) + static_cast<size_t>(row) * d * out_bytes, n.out_type, 1.f, lane);
     row += stride;
     if (row >= rows) break;
@@ -331,8 +317,8 @@ __global__ void __launch_bounds__(kHeadsWarps * 32) heads_kernel(HeadsParams p, 
   if (warp == 0) {
     Row r;
     r.load(p.x + row0 * d, lane);
-    r.layernorm(p.final_g, p.final_b, p.eps, d, lane);
-    r.layernorm(p.value_g, p.value_b, p.eps, d, lane);
+    ln_apply(r, p.final_g, p.final_b, ln_stats(r, d, p.eps), lane);
+    ln_apply(r, p.value_g, p.value_b, ln_stats(r, d, p.eps), lane);
     r.store_act(static_cast<__nv_bfloat16*>(p.value_in) + static_cast<size_t>(pos) * d, ActType::kBf16, 1.f, lane);
   }
 
@@ -345,15 +331,15 @@ __global__ void __launch_bounds__(kHeadsWarps * 32) heads_kernel(HeadsParams p, 
       const int square = action / kPlanes, plane = action - square * kPlanes;
       Row r;
       r.load(p.x + (row0 + p.square_start + square) * d, lane);
-      r.layernorm(p.final_g, p.final_b, p.eps, d, lane);
-      r.layernorm(p.policy_g, p.policy_b, p.eps, d, lane);
-      const float* w = p.policy_w + static_cast<size_t>(plane) * d;
-      float acc = 0.f;
+      ln_apply(r, p.final_g, p.final_b, ln_stats(r, d, p.eps), lane);
+      ln_apply(r, p.policy_g, p.policy_b, ln_stats(r, d, p.eps), lane);
+      Row w;  // the plane's weight row, vector loads
+      w.load(p.policy_w + static_cast<size_t>(plane) * d, lane);
+      float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < Row::kChunks; ++c)
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) acc += r.v[c * VEC + e] * __ldg(w + Row::col(c, lane) + e);
-      logit = warp_sum(acc) + __ldg(p.policy_bias + plane);
+      for (int k = 0; k < VPL; k += 2)
+        acc = fma2(make_float2(r.v[k], r.v[k + 1]), make_float2(w.v[k], w.v[k + 1]), acc);
+      logit = warp_sum(acc.x + acc.y) + __ldg(p.policy_bias + plane);
     }
     if (lane == 0) {
       if (p.softmax)
@@ -448,7 +434,7 @@ template <int VPL, int VEC>
 struct EmbedLaunch {
   static cudaError_t run(int d, const EmbedParams& e, const NormParams& n, int positions, cudaStream_t s) {
     const int rows = positions * e.t;
-    embed_ln_kernel<VPL, VEC><<<(rows + 7) / 8, 256, 0, s>>>(e, n, rows, d);
+    embed_ln_kernel<VPL, VEC><<<(rows + 7) / 8, 256, 2 * d * sizeof(float), s>>>(e, n, rows, d);
     return cudaGetLastError();
   }
 };
