@@ -31,6 +31,9 @@ sys.path.insert(0, str(ROOT))
 # stdout carries exactly one JSON line: keep NCCL's version banner off it.
 if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
     os.environ["NCCL_DEBUG"] = "WARN"
+# NCCL writes its log (the version line included, at WARN) to stdout unless told otherwise; stdout
+# carries only the JSON line.
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
 # DRAM bytes (read + write) of all GEMM launches of one forward pass, per position: ncu
 # dram__bytes_read.sum + dram__bytes_write.sum summed over the 49 GEMM launches of one pass of
