@@ -126,8 +126,9 @@ def test_residual_epilogue(cuda, fp8, m, n, k):
     delta = (af @ bf.T) * scale + bias
     ref = x0.float() + delta
     # the f16 sum of x and the f16-rounded update: at most an f16 half-ulp of each, plus the
-    # GEMM's own accumulation order where x and the update cancel
-    _within(x.float(), ref, (ref.abs() + delta.abs()) * 2 ** -10 + 1e-6, "residual")
+    # GEMM's own accumulation order where x and the update cancel; a sum below f16's smallest
+    # normal (2^-14) may come back flushed to zero from the L2's f16 reduce-add
+    _within(x.float(), ref, (ref.abs() + delta.abs()) * 2 ** -10 + 2 ** -14, "residual")
 
 
 def test_rows_beyond_m_untouched(cuda):
