@@ -286,6 +286,9 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
   // CTA pairs halve the operand bytes per FLOP, which pays where the main loop is long (FFN2,
   // K = 4d); with K = d the two CTAs' coupled epilogues cost more than that saves.
   plan->pair = pair_enabled() && args.n % 256 == 0 && args.k >= 1024;
+  // The memory-bound residual GEMMs with a short K (out-proj) run 128-column tiles with four
+  // TMEM accumulators: the reduce-add stores drain behind three tiles of MMAs.
+  if (!plan->pair && args.epi == Epilogue::kResidual && args.k < 1024 && args.n % 128 == 0) plan->bn = 128;
   if (!make_kmajor_map(&plan->map_a, args.a, eb, args.m, args.k, kTileM) ||
       !make_kmajor_map(&plan->map_b, args.b, eb, args.n, args.k, plan->pair ? 128 : plan->bn)) {
     snprintf(err, 256, "gemm: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", args.m, args.n, args.k);

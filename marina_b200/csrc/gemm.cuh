@@ -10,8 +10,9 @@
 //   warp 0, one lane : TMA producer. A 128x128-byte tile and a BNx128-byte tile per stage,
 //                      128-byte swizzled, into a STAGES-deep ring of shared-memory buffers.
 //   warp 1, one lane : MMA issuer. 4 tcgen05.mma (K = 32 bytes each) per stage into a TMEM
-//                      accumulator; two accumulators of BN columns alternate between tiles
-//                      so the epilogue of one tile overlaps the MMAs of the next.
+//                      accumulator; two accumulators of BN columns (four for BN <= 128)
+//                      cycle between tiles so the epilogue of one tile overlaps the MMAs of
+//                      the next.
 //   warps 2..        : epilogue (8 warps, 16 for the GELU epilogue). Warp w reads TMEM lanes
 //                      32*(w%4).. (one output row per thread) in its share of the tile's
 //                      columns, 32 at a time, applies the epilogue functor, writes the
@@ -297,6 +298,9 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
   constexpr int kEpiBytes = S::kEpiBytes;
   constexpr int kElemsPerStage = FP8 ? 128 : 64;
   constexpr uint32_t kIdesc = FP8 ? idesc_e4m3(kTileM, BN) : idesc_bf16(kTileM, BN);
+  // TMEM accumulators cycled between tiles: four of 128 columns for BN <= 128 (the epilogue
+  // may trail the MMAs by three tiles), else two.
+  constexpr int kAccs = BN <= 128 ? 4 : 2;
   constexpr int kRowBytes = kEpiChunk * Epi::kOutBytes;  // staged bytes per output row
 
   extern __shared__ uint8_t smem_raw[];
@@ -308,9 +312,9 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm_epi + kEpiBytes);
   uint64_t* full = bars;                      // [kStages] TMA -> MMA
   uint64_t* empty = bars + kStages;           // [kStages] MMA -> TMA
-  uint64_t* tmem_full = bars + 2 * kStages;   // [2] MMA -> epilogue
-  uint64_t* tmem_empty = tmem_full + 2;       // [2] epilogue -> MMA
-  uint64_t* drain = tmem_empty + 2;           // [1] MMA completion on abort
+  uint64_t* tmem_full = bars + 2 * kStages;   // [kAccs] MMA -> epilogue
+  uint64_t* tmem_empty = tmem_full + kAccs;   // [kAccs] epilogue -> MMA
+  uint64_t* drain = tmem_empty + kAccs;       // [1] MMA completion on abort
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -326,7 +330,7 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < kAccs; ++a) {
       mbar_init(&tmem_full[a], 1);
       mbar_init(&tmem_empty[a], kEpiWarps);
     }
@@ -420,8 +424,10 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
         }
         if (!ok) break;
         tc_commit(&tmem_full[acc]);
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1u;
+        if (++acc == kAccs) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
       }
       if (*abort && issued) {
         // Let the MMAs already issued finish before their buffers and TMEM go away.
@@ -488,8 +494,10 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&tmem_empty[acc]);
       }
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
+      if (++acc == kAccs) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
