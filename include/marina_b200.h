@@ -215,6 +215,17 @@ MRN_API int mrn_test_gemm(int fp8, int epilogue, const void* a, const void* b, c
 MRN_API int mrn_test_gemm_ln(int fp8, const void* a, const void* b, const float* bias, const float* gamma,
                              const float* beta, void* x, void* h, int m, int d, int k, float scale, float eps,
                              float inv_q, int* status, void* stream);
+/* One GEMM whose A operand is the LayerNorm of the f16 rows x[m,k], computed inside the kernel
+ * (the kernel that serves norm1 -> QKV and norm2 -> FFN1 for e4m3 operands, k = 512, n a multiple
+ * of 256): A = e4m3 codes of (LN(x) * gamma + beta) * a_inv_q (eps), then as mrn_test_gemm with
+ * `epilogue` 0 (bias->bf16), 2 (GELU->e4m3) or 6 (tanh GELU->e4m3) on e4m3 `b`. */
+MRN_API int mrn_test_gemm_norm(int epilogue, const void* x, const float* gamma, const float* beta, float eps,
+                               float a_inv_q, const void* b, const float* bias, void* out, int ldo, int m, int n,
+                               int k, float scale, float inv_q, int* status, void* stream);
+/* The LayerNorm kernel on its own: out[rows,d] = LN(x) * gamma + beta from f16 x, as bf16, or
+ * with `e4m3` as e4m3 codes of the value * inv_q. */
+MRN_API int mrn_test_layernorm(const void* x, const float* gamma, const float* beta, float eps, int e4m3,
+                               float inv_q, void* out, int rows, int d, void* stream);
 MRN_API const char* mrn_test_last_error(void);
 
 #ifdef __cplusplus

@@ -6,6 +6,7 @@
 
 #include "../../include/marina_b200.h"
 #include "gemm.h"
+#include "kernels.cuh"
 
 namespace {
 thread_local char g_test_error[512];
@@ -93,6 +94,42 @@ int mrn_test_gemm_ln(int fp8, const void* a, const void* b, const float* bias, c
   args.ln_e4m3 = fp8 != 0;
   args.ln_inv_q = inv_q;
   return run(args, stream);
+}
+
+int mrn_test_gemm_norm(int epilogue, const void* x, const float* gamma, const float* beta, float eps, float a_inv_q,
+                       const void* b, const float* bias, void* out, int ldo, int m, int n, int k, float scale,
+                       float inv_q, int* status, void* stream) {
+  if (!prepare()) return fail("gemm_prepare_device failed");
+  mrn::GemmArgs args;
+  args.b = b;
+  args.m = m;
+  args.n = n;
+  args.k = k;
+  args.fp8 = true;
+  args.epi = static_cast<mrn::Epilogue>(epilogue);
+  args.out = out;
+  args.ldo = ldo;
+  args.bias = bias;
+  args.scale = scale;
+  args.inv_q = inv_q;
+  args.status = status;
+  args.norm_x = x;
+  args.gamma = gamma;
+  args.beta = beta;
+  args.eps = eps;
+  args.ln_inv_q = a_inv_q;
+  return run(args, stream);
+}
+
+int mrn_test_layernorm(const void* x, const float* gamma, const float* beta, float eps, int e4m3, float inv_q,
+                       void* out, int rows, int d, void* stream) {
+  const mrn::NormParams np{gamma, beta, eps, out, e4m3 ? mrn::ActType::kE4m3 : mrn::ActType::kBf16, inv_q};
+  const cudaError_t e = mrn::launch_layernorm(static_cast<const __half*>(x), np, rows, d, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    snprintf(g_test_error, sizeof(g_test_error), "layernorm launch: %s", cudaGetErrorString(e));
+    return MRN_ERR_CUDA;
+  }
+  return MRN_OK;
 }
 
 }  // extern "C"

@@ -5,6 +5,7 @@
 #include "gemm.cuh"
 #include "gemm.h"
 #include "gemm_ln.cuh"
+#include "gemm_norm.cuh"
 #include "tmap.h"
 
 namespace mrn {
@@ -196,6 +197,56 @@ cudaError_t prepare_ln() {
                               LnShape<BN>::kSmemBytes);
 }
 
+// ---- GEMM with the LayerNorm of A in the kernel (gemm_norm.cuh)
+template <class Epi>
+cudaError_t launch_norm(const GemmPlan& p, const Epi& epi, cudaStream_t stream) {
+  using S = NormShape<Epi::kOutBytes, Epi::kWarps>;
+  const GemmArgs& a = p.args;
+  const NormA na{static_cast<const __half*>(a.norm_x), a.gamma, a.beta, a.eps, a.ln_inv_q};
+  gemm_norm_kernel<Epi><<<p.grid, S::kThreads, S::kSmemBytes, stream>>>(p.map_b, p.map_out, epi, na, a.m, a.n,
+                                                                        a.status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_norm_epi(const GemmPlan& p, cudaStream_t stream) {
+  const GemmArgs& a = p.args;
+  switch (a.epi) {
+    case Epilogue::kBias: return launch_norm(p, EpiBiasBf16{a.bias, a.scale}, stream);
+    case Epilogue::kGeluE4m3: return launch_norm(p, EpiGelu<true>{a.bias, a.scale, a.inv_q}, stream);
+    case Epilogue::kGeluTanhE4m3: return launch_norm(p, EpiGeluTanh<true>{a.bias, a.scale, a.inv_q}, stream);
+    default: break;
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <class Epi>
+cudaError_t prepare_norm() {
+  return cudaFuncSetAttribute(gemm_norm_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              NormShape<Epi::kOutBytes, Epi::kWarps>::kSmemBytes);
+}
+
+bool plan_norm(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
+  if (!gemm_norm_supported(args)) {
+    snprintf(err, 256, "gemm+norm: needs e4m3, K=%d, N%%256==0, bias/e4m3-GELU epilogue, aligned buffers (M=%d N=%d K=%d)",
+             kNormK, args.m, args.n, args.k);
+    return false;
+  }
+  plan->norm = true;
+  plan->bn = 256;
+  const bool e4m3_out = args.epi != Epilogue::kBias;
+  if (!make_kmajor_map(&plan->map_b, args.b, 1, args.n, args.k, 128) ||
+      !make_store_map(&plan->map_out, args.out,
+                      e4m3_out ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, e4m3_out ? 1 : 2,
+                      args.m, args.n, args.ldo)) {
+    snprintf(err, 256, "gemm+norm: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", args.m, args.n, args.k);
+    return false;
+  }
+  const int units = ((args.m + 2 * kTileM - 1) / (2 * kTileM)) * (args.n / 256);
+  const int pairs = num_sms / 2;
+  plan->grid = 2 * (units < pairs ? units : pairs);
+  return true;
+}
+
 bool plan_ln(GemmPlan* plan, const GemmArgs& args, char* err) {
   const int eb = args.fp8 ? 1 : 2;
   plan->bn = gemm_ln_pick_bn(args.n);
@@ -238,6 +289,14 @@ int gemm_ln_pick_bn(int n) {
   return 0;
 }
 
+bool gemm_norm_supported(const GemmArgs& a) {
+  auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  return a.fp8 && a.k == kNormK && a.m > 0 && a.n > 0 && a.n % 256 == 0 && a.ldo >= a.n && a.ldo % 16 == 0 &&
+         (a.epi == Epilogue::kBias || a.epi == Epilogue::kGeluE4m3 || a.epi == Epilogue::kGeluTanhE4m3) && a.norm_x &&
+         a.gamma && a.beta && a.bias && a.out && aligned(a.norm_x) && aligned(a.gamma) && aligned(a.beta) &&
+         aligned(a.bias) && aligned(a.out);
+}
+
 int gemm_pick_bn(int n) {
   for (int bn : {256, 192, 128, 64})
     if (n % bn == 0) return bn;
@@ -247,7 +306,9 @@ int gemm_pick_bn(int n) {
 bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
   plan->args = args;
   plan->pair = false;
+  plan->norm = false;
   plan->cluster = 0;
+  if (args.norm_x) return plan_norm(plan, args, num_sms, err);
   if (args.epi == Epilogue::kResidualLn) {
     if (args.m <= 0 || args.k <= 0 || (args.k * (args.fp8 ? 1 : 2)) % 16 != 0 ||
         (reinterpret_cast<uintptr_t>(args.out) & 15) != 0 || (reinterpret_cast<uintptr_t>(args.bias) & 15) != 0) {
@@ -342,10 +403,14 @@ cudaError_t gemm_prepare_device() {
   if ((e = prepare_ln<128>()) != cudaSuccess) return e;
   if ((e = prepare_ln<96>()) != cudaSuccess) return e;
   if ((e = prepare_ln<64>()) != cudaSuccess) return e;
+  if ((e = prepare_norm<EpiBiasBf16>()) != cudaSuccess) return e;
+  if ((e = prepare_norm<EpiGelu<true>>()) != cudaSuccess) return e;
+  if ((e = prepare_norm<EpiGeluTanh<true>>()) != cudaSuccess) return e;
   return prepare_bn<64>();
 }
 
 cudaError_t gemm_launch(const GemmPlan& plan, cudaStream_t stream) {
+  if (plan.norm) return launch_norm_epi(plan, stream);
   if (plan.args.epi == Epilogue::kResidualLn) return launch_ln(plan, stream);
   if (plan.pair) return plan.args.fp8 ? launch_pair_epi<true>(plan, stream) : launch_pair_epi<false>(plan, stream);
   return plan.args.fp8 ? launch_fp8<true>(plan, stream) : launch_fp8<false>(plan, stream);

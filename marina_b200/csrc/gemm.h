@@ -30,13 +30,18 @@ struct GemmArgs {
   float scale = 1.f;         // dequantisation of the accumulator (weight scale x activation scale)
   float inv_q = 1.f;         // 1 / output quantisation scale (kGeluE4m3)
   int* status = nullptr;     // device error word (first error wins)
-  // kResidualLn only: the LayerNorm of the updated rows of `out` (N = d, ldo = d)
-  const float* gamma = nullptr;  // [N]
-  const float* beta = nullptr;   // [N]
+  // kResidualLn: the LayerNorm of the updated rows of `out` (N = d, ldo = d). With `norm_x`:
+  // the LayerNorm that produces A (K = d).
+  const float* gamma = nullptr;  // [N], or [K] with norm_x
+  const float* beta = nullptr;   // [N], or [K] with norm_x
   float eps = 1e-5f;
   void* ln_out = nullptr;        // h [M, N], bf16 or e4m3
   bool ln_e4m3 = false;
-  float ln_inv_q = 1.f;          // 1 / e4m3 scale of h
+  float ln_inv_q = 1.f;          // 1 / e4m3 scale of h (kResidualLn) or of the normalised A
+  // Normalised A (e4m3 operands, K = 512, N a multiple of 256; epilogues kBias, kGeluE4m3,
+  // kGeluTanhE4m3): A = e4m3((LN(norm_x) * gamma + beta) * ln_inv_q) is computed inside the
+  // kernel from the f16 residual stream norm_x [M, K], and `a` is not read.
+  const void* norm_x = nullptr;
 };
 
 struct GemmPlan {
@@ -49,6 +54,7 @@ struct GemmPlan {
   bool pair = false;  // 256 x 256 tiles on CTA pairs (tcgen05 cta_group::2)
   CUtensorMap map_aux;  // kResidualLn: the h store map
   int cluster = 0;      // kResidualLn: CTAs per row block (N / bn)
+  bool norm = false;    // A normalised in the kernel (gemm_norm.cuh)
 };
 
 // Widest supported N tile (256, 192, 128, 64) dividing n; 0 if none. Plans for N a multiple of
@@ -57,6 +63,10 @@ int gemm_pick_bn(int n);
 
 // kResidualLn: the N slice of one CTA (128, 96 or 64 dividing n with n / slice <= 8); 0 if none.
 int gemm_ln_pick_bn(int n);
+
+// Whether gemm_plan accepts `norm_x` for this shape and epilogue (the kernel is instantiated for
+// K = 512 only).
+bool gemm_norm_supported(const GemmArgs& args);
 
 // Validate shapes and alignment and build the tensor maps. `err` (>= 256 bytes) receives a
 // message on failure.

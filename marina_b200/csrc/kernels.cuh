@@ -34,7 +34,7 @@ struct NormParams {
   float inv_q;     // 1 / e4m3 scale
 };
 
-// x = tokens(boards); out = LN(x) (layer 0's norm1) in one pass.
+// x = tokens(boards); out = LN(x) (layer 0's norm1) in one pass, or x alone when n.out is null.
 cudaError_t launch_embed_ln(const EmbedParams& e, const NormParams& n, int positions, int d, cudaStream_t s);
 // out = LN(x) for rows [0, rows).
 cudaError_t launch_layernorm(const __half* x, const NormParams& n, int rows, int d, cudaStream_t s);

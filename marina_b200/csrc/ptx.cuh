@@ -24,6 +24,8 @@ enum DeviceError : int {
   kErrTimeoutEpilogue = 3,
   kErrTimeoutDrain = 4,
   kErrTimeoutExchange = 5,  // a row-statistics exchange between the CTAs of a cluster
+  // 6: attention.cu's producer/consumer handshake
+  kErrTimeoutNorm = 7,      // a norm warp of the normalised-A GEMM waiting for its A buffer
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

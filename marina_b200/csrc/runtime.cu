@@ -248,38 +248,80 @@ bool ln_fusion_enabled() {
   return on;
 }
 
-void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool fuse, GemmArgs (&g)[4]) {
+bool norm_a_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("MRN_GEMM_NORM");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
+namespace {
+
+GemmArgs base_args(const mrn_ctx* c, int rows) {
+  GemmArgs a;
+  a.m = rows;
+  a.fp8 = c->precision == MRN_PRECISION_FP8;
+  a.status = c->status;
+  a.eps = c->eps;
+  a.ln_e4m3 = a.fp8;
+  return a;
+}
+
+float gemm_scale(const mrn_ctx* c, const DevLayer& D, int i) {
+  return c->precision == MRN_PRECISION_FP8 ? D.ws[i] * D.as[i] : D.ws[i];
+}
+
+// A normalised in the kernel from x with (gamma, beta) and the activation scale of the norm's
+// output, kept only where the normalised-A kernel supports the GEMM.
+void try_norm(GemmArgs& g, const LayerBuffers& b, const float* gamma, const float* beta, float act_scale) {
+  GemmArgs n = g;
+  n.norm_x = b.x, n.gamma = gamma, n.beta = beta, n.ln_inv_q = 1.f / act_scale;
+  if (gemm_norm_supported(n)) g = n;
+}
+
+// QKV: h (or norm1(x)) -> qkv (bf16)
+void qkv_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool norm, GemmArgs& g) {
+  const DevLayer& D = c->dl[l];
+  g = base_args(c, rows);
+  g.a = b.h, g.b = D.w_qkv, g.n = 3 * c->d, g.k = c->d, g.epi = Epilogue::kBias, g.out = b.qkv;
+  g.ldo = 3 * c->d, g.bias = D.b_qkv, g.scale = gemm_scale(c, D, 0);
+  if (norm) try_norm(g, b, D.n1g, D.n1b, D.as[0]);
+}
+
+}  // namespace
+
+bool qkv_normalises(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool norm) {
+  GemmArgs g;
+  qkv_args(c, l, rows, b, norm, g);
+  return g.norm_x != nullptr;
+}
+
+void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool fuse, bool norm,
+                     GemmArgs (&g)[4]) {
   const int d = c->d, ff = c->dff;
   const bool fp8 = c->precision == MRN_PRECISION_FP8;
   const DevLayer& D = c->dl[l];
-  auto scale = [&](int i) { return fp8 ? D.ws[i] * D.as[i] : D.ws[i]; };
-  GemmArgs base;
-  base.m = rows;
-  base.fp8 = fp8;
-  base.status = c->status;
-  base.eps = c->eps;
-  base.ln_e4m3 = fp8;
-  for (GemmArgs& a : g) a = base;
-  // QKV: h -> qkv (bf16)
-  g[0].a = b.h, g[0].b = D.w_qkv, g[0].n = 3 * d, g[0].k = d, g[0].epi = Epilogue::kBias, g[0].out = b.qkv;
-  g[0].ldo = 3 * d, g[0].bias = D.b_qkv, g[0].scale = scale(0);
-  // out-proj: attn -> x += (then h = norm2(x))
-  g[1].a = b.attn, g[1].b = D.w_o, g[1].n = d, g[1].k = d, g[1].epi = Epilogue::kResidual, g[1].out = b.x;
-  g[1].ldo = d, g[1].bias = D.b_o, g[1].scale = scale(1);
-  if (fuse) {
-    g[1].epi = Epilogue::kResidualLn, g[1].gamma = D.n2g, g[1].beta = D.n2b, g[1].ln_out = b.h;
-    g[1].ln_inv_q = 1.f / D.as[2];
-  }
-  // FFN1: h -> ff = GELU(.), the card's form (the value head's GELU is always the erf one)
+  qkv_args(c, l, rows, b, norm, g[0]);
+  for (int i = 1; i < 4; ++i) g[i] = base_args(c, rows);
+  // FFN1: h (or norm2(x)) -> ff = GELU(.), the card's form (the value head's GELU is always the erf one)
   const bool tanh_form = c->gelu == MRN_GELU_TANH;
   g[2].a = b.h, g[2].b = D.w_1, g[2].n = ff, g[2].k = d;
   g[2].epi = fp8 ? (tanh_form ? Epilogue::kGeluTanhE4m3 : Epilogue::kGeluE4m3)
                  : (tanh_form ? Epilogue::kGeluTanhBf16 : Epilogue::kGeluBf16);
-  g[2].out = b.ff, g[2].ldo = ff, g[2].bias = D.b_1, g[2].scale = scale(2), g[2].inv_q = 1.f / D.as[3];
-  // FFN2: ff -> x += (then h = norm1 of the next layer)
+  g[2].out = b.ff, g[2].ldo = ff, g[2].bias = D.b_1, g[2].scale = gemm_scale(c, D, 2), g[2].inv_q = 1.f / D.as[3];
+  if (norm) try_norm(g[2], b, D.n2g, D.n2b, D.as[2]);
+  // out-proj: attn -> x += (then h = norm2(x), unless FFN1 normalises x itself)
+  g[1].a = b.attn, g[1].b = D.w_o, g[1].n = d, g[1].k = d, g[1].epi = Epilogue::kResidual, g[1].out = b.x;
+  g[1].ldo = d, g[1].bias = D.b_o, g[1].scale = gemm_scale(c, D, 1);
+  if (fuse && !g[2].norm_x) {
+    g[1].epi = Epilogue::kResidualLn, g[1].gamma = D.n2g, g[1].beta = D.n2b, g[1].ln_out = b.h;
+    g[1].ln_inv_q = 1.f / D.as[2];
+  }
+  // FFN2: ff -> x += (then h = norm1 of the next layer, unless its QKV normalises x itself)
   g[3].a = b.ff, g[3].b = D.w_2, g[3].n = d, g[3].k = ff, g[3].epi = Epilogue::kResidual, g[3].out = b.x;
-  g[3].ldo = d, g[3].bias = D.b_2, g[3].scale = scale(3);
-  if (fuse && l + 1 < c->layers) {
+  g[3].ldo = d, g[3].bias = D.b_2, g[3].scale = gemm_scale(c, D, 3);
+  if (fuse && l + 1 < c->layers && !qkv_normalises(c, l + 1, rows, b, norm)) {
     const DevLayer& N = c->dl[l + 1];
     g[3].epi = Epilogue::kResidualLn, g[3].gamma = N.n1g, g[3].beta = N.n1b, g[3].ln_out = b.h;
     g[3].ln_inv_q = 1.f / N.as[0];
@@ -300,21 +342,24 @@ namespace {
 
 // GEMM plans of one bucket: per layer QKV, out-proj, FFN1, FFN2; then value ff1. A residual GEMM
 // whose fused LayerNorm cannot be planned on this device falls back to the plain residual
-// epilogue followed by a LayerNorm launch.
+// epilogue followed by a LayerNorm launch; where the consuming GEMM normalises x itself, no
+// LayerNorm launch is needed at all.
 int make_plans(mrn_ctx* c, Bucket& b) {
-  const int M = b.positions * c->t, d = c->d;
+  const int M = b.positions * c->t, d = c->d, L = c->layers;
   char err[256];
   const mrn::LayerBuffers bufs{c->h, c->qkv, c->attn, c->ff, c->x};
-  const bool fuse = mrn::ln_fusion_enabled();
-  b.fused.assign(2 * c->layers, 0);
-  for (int l = 0; l < c->layers; ++l) {
+  const bool fuse = mrn::ln_fusion_enabled(), norm = mrn::norm_a_enabled();
+  b.ln_launch.assign(2 * L, 0);
+  b.embed_norm = !mrn::qkv_normalises(c, 0, M, bufs, norm);
+  for (int l = 0; l < L; ++l) {
     GemmArgs g[4];
-    mrn::layer_gemm_args(c, l, M, bufs, fuse, g);
+    mrn::layer_gemm_args(c, l, M, bufs, fuse, norm, g);
+    bool ln_in_epilogue[2] = {false, false};
     for (int i = 0; i < 4; ++i) {
       GemmPlan p;
       if (g[i].epi == Epilogue::kResidualLn) {
         if (mrn::gemm_plan(&p, g[i], c->num_sms, err)) {
-          b.fused[2 * l + (i == 1 ? 0 : 1)] = 1;
+          ln_in_epilogue[i == 1 ? 0 : 1] = true;
           b.plans.push_back(p);
           continue;
         }
@@ -323,6 +368,8 @@ int make_plans(mrn_ctx* c, Bucket& b) {
       if (!mrn::gemm_plan(&p, g[i], c->num_sms, err)) return c->fail(MRN_ERR_UNSUPPORTED, "layer %d: %s", l, err);
       b.plans.push_back(p);
     }
+    b.ln_launch[2 * l] = !ln_in_epilogue[0] && !g[2].norm_x;
+    b.ln_launch[2 * l + 1] = l + 1 < L && !ln_in_epilogue[1] && !mrn::qkv_normalises(c, l + 1, M, bufs, norm);
   }
   GemmArgs v;
   v.m = b.positions, v.n = d, v.k = d, v.fp8 = false, v.status = c->status;
@@ -347,7 +394,8 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
   mrn::EmbedParams e{c->boards, c->piece, c->square, c->state, c->cast_w, c->cast_b, c->ep, c->x, c->t, c->square_start};
   const DevLayer& D0 = c->dl[0];
   mark(MRN_PROFILE_EMBED);
-  CK(mrn::launch_embed_ln(e, mrn::NormParams{D0.n1g, D0.n1b, c->eps, c->h, act, 1.f / D0.as[0]}, P, d, s));
+  CK(mrn::launch_embed_ln(
+      e, mrn::NormParams{D0.n1g, D0.n1b, c->eps, b.embed_norm ? c->h : nullptr, act, 1.f / D0.as[0]}, P, d, s));
   done();
   const mrn::LayerBuffers bufs{c->h, c->qkv, c->attn, c->ff, c->x};
   for (int l = 0; l < c->layers; ++l) {
@@ -363,7 +411,7 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
     mark(MRN_PROFILE_GEMM);
     CK(mrn::gemm_launch(plans[1], s));
     done();
-    if (!b.fused[2 * l]) {
+    if (b.ln_launch[2 * l]) {
       mark(MRN_PROFILE_LAYERNORM);
       CK(mrn::launch_site_layernorm(c, l, 0, bufs, R, s));
       done();
@@ -372,7 +420,7 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
     CK(mrn::gemm_launch(plans[2], s));
     CK(mrn::gemm_launch(plans[3], s));
     done();
-    if (l + 1 < c->layers && !b.fused[2 * l + 1]) {
+    if (b.ln_launch[2 * l + 1]) {
       mark(MRN_PROFILE_LAYERNORM);
       CK(mrn::launch_site_layernorm(c, l, 1, bufs, R, s));
       done();
@@ -394,11 +442,11 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
   return MRN_OK;
 }
 
-// Embedding + LayerNorm, 5 per layer (QKV, attention, out-proj, FFN1, FFN2), a LayerNorm after each
-// residual GEMM that does not carry it (norm2, and norm1 of every layer but the first), 3 for the heads.
+// Embedding, 5 per layer (QKV, attention, out-proj, FFN1, FFN2), a LayerNorm launch wherever no GEMM
+// computes that norm (norm2, and norm1 of every layer but the first), 3 for the heads.
 int launches_per_forward(const mrn_ctx* c, const Bucket& b) {
   int n = 1 + 5 * c->layers + 3;
-  for (int l = 0; l < c->layers; ++l) n += (b.fused[2 * l] ? 0 : 1) + (l + 1 < c->layers && !b.fused[2 * l + 1]);
+  for (uint8_t launch : b.ln_launch) n += launch;
   return n;
 }
 

@@ -32,9 +32,11 @@ struct DevLayer {
 struct Bucket {
   int positions = 0;
   std::vector<GemmPlan> plans;  // 4 per layer, then the value head's first layer
-  // Per layer: [2l] out-proj carries norm2, [2l+1] FFN2 carries the next layer's norm1 (the
-  // fused residual + LayerNorm epilogue); where 0, a LayerNorm launch follows the GEMM.
-  std::vector<uint8_t> fused;
+  // Per layer: [2l] a LayerNorm launch (norm2) follows out-proj, [2l+1] one (the next layer's
+  // norm1) follows FFN2. 0 where the norm runs inside a GEMM: in the consuming GEMM's A operand
+  // (gemm_norm.cuh) or in the residual GEMM's epilogue (gemm_ln.cuh).
+  std::vector<uint8_t> ln_launch;
+  bool embed_norm = true;  // the embedding kernel writes layer 0's norm1 (its QKV does not normalise A)
   cudaGraphExec_t graph = nullptr;
 };
 
@@ -127,12 +129,19 @@ struct mrn_ctx {
 };
 
 namespace mrn {
-// The four GEMMs of layer `l` over `rows` rows: QKV, out-proj, FFN1, FFN2. With `fuse`, out-proj
-// carries norm2 and FFN2 (all layers but the last) the next layer's norm1 as the fused residual +
-// LayerNorm epilogue.
-void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool fuse, GemmArgs (&g)[4]);
-// Whether plans use the fused residual + LayerNorm epilogue (environment MRN_GEMM_LN=0 / 1 overrides).
+// The four GEMMs of layer `l` over `rows` rows: QKV, out-proj, FFN1, FFN2. With `norm`, QKV and
+// FFN1 compute norm1 / norm2 of x themselves where the normalised-A kernel supports the shape.
+// With `fuse`, out-proj carries norm2 and FFN2 (all layers but the last) the next layer's norm1 as
+// the fused residual + LayerNorm epilogue, unless the consuming GEMM normalises A itself.
+void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool fuse, bool norm,
+                     GemmArgs (&g)[4]);
+// Whether layer l's QKV GEMM computes norm1 itself (under the same `norm` setting).
+bool qkv_normalises(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool norm);
+// Whether plans use the fused residual + LayerNorm epilogue (environment MRN_GEMM_LN=1; off by default).
 bool ln_fusion_enabled();
+// Whether QKV and FFN1 normalise their A operand in the kernel (environment MRN_GEMM_NORM=1; off by
+// default: the CTA-pair kernel it needs is slower at K = d than LayerNorm launch + single-CTA GEMM).
+bool norm_a_enabled();
 // The LayerNorm launch that stands in for an unfused site: norm2 of layer `l` (site 0) or norm1 of
 // layer l + 1 (site 1), from x into h.
 cudaError_t launch_site_layernorm(const mrn_ctx* c, int l, int site, const LayerBuffers& b, int rows,

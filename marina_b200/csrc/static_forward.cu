@@ -103,9 +103,10 @@ int gemm(mrn_ctx* c, const mrn::GemmArgs& a, cudaStream_t s) {
 }
 
 // A residual GEMM and the LayerNorm after it (norm2 of layer l at site 0, norm1 of layer l + 1 at
-// site 1; none after the last layer): fused where it plans, else the residual epilogue and a
-// LayerNorm launch.
-int residual(mrn_ctx* c, int l, int site, mrn::GemmArgs a, const mrn::LayerBuffers& b, cudaStream_t s) {
+// site 1): in the epilogue where that plans, else the plain residual GEMM followed by a LayerNorm
+// launch when the next GEMM reads h (`need_h`: not after the last layer, nor where the next GEMM
+// normalises x itself).
+int residual(mrn_ctx* c, int l, int site, mrn::GemmArgs a, const mrn::LayerBuffers& b, bool need_h, cudaStream_t s) {
   mrn::GemmPlan p;
   char err[256];
   if (a.epi == mrn::Epilogue::kResidualLn) {
@@ -117,12 +118,10 @@ int residual(mrn_ctx* c, int l, int site, mrn::GemmArgs a, const mrn::LayerBuffe
   }
   if (!mrn::gemm_plan(&p, a, c->num_sms, err)) return c->fail(MRN_ERR_UNSUPPORTED, "%s", err);
   CKS(mrn::gemm_launch(p, s));
-  if (site == 0 || l + 1 < c->layers) CKS(mrn::launch_site_layernorm(c, l, site, b, a.m, s));
+  if (need_h) CKS(mrn::launch_site_layernorm(c, l, site, b, a.m, s));
   return MRN_OK;
 }
 
-// The forward pass of the graph path (embed, layers, heads), with the array's buffers and the
-// caller's inputs and outputs.
 int forward(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, float* priors, float* wdl, uint8_t* base,
             cudaStream_t s) {
   using mrn::ActType;
@@ -140,21 +139,24 @@ int forward(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, floa
   int rc;
 
   const mrn::DevLayer& D0 = c->dl[0];
+  const mrn::LayerBuffers bufs{h, qkv, attn, ff, x};
+  const bool fuse = mrn::ln_fusion_enabled(), norm = mrn::norm_a_enabled();
   CKS(mrn::launch_embed_ln(
       mrn::EmbedParams{boards, c->piece, c->square, c->state, c->cast_w, c->cast_b, c->ep, x, c->t, c->square_start},
-      mrn::NormParams{D0.n1g, D0.n1b, c->eps, h, act, 1.f / D0.as[0]}, n, d, s));
-  const mrn::LayerBuffers bufs{h, qkv, attn, ff, x};
-  const bool fuse = mrn::ln_fusion_enabled();
+      mrn::NormParams{D0.n1g, D0.n1b, c->eps, mrn::qkv_normalises(c, 0, R, bufs, norm) ? nullptr : h, act,
+                      1.f / D0.as[0]},
+      n, d, s));
   for (int l = 0; l < c->layers; ++l) {
     const mrn::DevLayer& D = c->dl[l];
     mrn::GemmArgs g[4];
-    mrn::layer_gemm_args(c, l, R, bufs, fuse, g);
+    mrn::layer_gemm_args(c, l, R, bufs, fuse, norm, g);
     if ((rc = gemm(c, g[0], s))) return rc;
     CKS(mrn::launch_attention(mrn::AttentionParams{qkv, attn, act, 1.f / D.as[1], c->t, d, c->heads, c->status}, n,
                               d / c->heads, s));
-    if ((rc = residual(c, l, 0, g[1], bufs, s))) return rc;
+    if ((rc = residual(c, l, 0, g[1], bufs, !g[2].norm_x, s))) return rc;
     if ((rc = gemm(c, g[2], s))) return rc;
-    if ((rc = residual(c, l, 1, g[3], bufs, s))) return rc;
+    const bool need_h = l + 1 < c->layers && !mrn::qkv_normalises(c, l + 1, R, bufs, norm);
+    if ((rc = residual(c, l, 1, g[3], bufs, need_h, s))) return rc;
   }
   mrn::HeadsParams hp;
   hp.x = x, hp.final_g = c->fn_g, hp.final_b = c->fn_b, hp.policy_g = c->pn_g, hp.policy_b = c->pn_b;

@@ -293,22 +293,39 @@ ev.close()
 """
 
 
-@pytest.mark.parametrize("net,precision", [("small", "bf16"), ("small", "fp8"), ("nano", "fp8w")])
-def test_fused_and_unfused_layernorm_plans(tmp_path, net, precision):
-    """The residual GEMMs with the following LayerNorm fused in (MRN_GEMM_LN=1, no LayerNorm
-    launches) and the plain residual GEMM + LayerNorm launches (MRN_GEMM_LN=0) agree, and both
-    meet the oracle bounds. Child processes: the switch is read once per process."""
+def _run_plans(tmp_path, net, precision, envs):
+    """FUSED_SCRIPT in one child process per environment override (the switches are read once per
+    process); returns {key: npz}."""
     import os
     import subprocess
     import sys
 
     outs = {}
-    for flag in ("0", "1"):
-        out = tmp_path / f"ln{flag}.npz"
-        env = dict(os.environ, MRN_GEMM_LN=flag)
+    for key, extra in envs.items():
+        out = tmp_path / f"{key}.npz"
+        env = dict(os.environ, **extra)
         subprocess.run([sys.executable, "-c", FUSED_SCRIPT, net, precision, str(out)], env=env, check=True,
                        cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))), timeout=600)
-        outs[flag] = np.load(out)
+        outs[key] = np.load(out)
+    return outs
+
+
+def _check_plans_against_oracle(outs, net, precision):
+    w = weights.random_init(card(net), seed=0)
+    boards, legal, counts, _ = chess.random_positions(41, 300, 0, 120)
+    ref_p, ref_w = oracle.OracleNetwork(card(net), weights.fp8_weights(w) if precision != "bf16" else w,
+                                        threads=16).evaluate(boards, legal)
+    for out in outs.values():
+        check(compare(out["priors"], out["wdl"], ref_p, ref_w, counts), precision)
+
+
+@pytest.mark.parametrize("net,precision", [("small", "bf16"), ("small", "fp8"), ("nano", "fp8w")])
+def test_fused_and_unfused_layernorm_plans(tmp_path, net, precision):
+    """The residual GEMMs with the following LayerNorm fused in (MRN_GEMM_LN=1, no LayerNorm
+    launches) and the plain residual GEMM + LayerNorm launches (MRN_GEMM_LN=0) agree, and both
+    meet the oracle bounds (QKV and FFN1 read h, MRN_GEMM_NORM=0)."""
+    outs = _run_plans(tmp_path, net, precision, {"0": {"MRN_GEMM_LN": "0", "MRN_GEMM_NORM": "0"},
+                                                 "1": {"MRN_GEMM_LN": "1", "MRN_GEMM_NORM": "0"}})
     layers = card(net).n_layers
     assert int(outs["0"]["launches"]) == 7 * layers + 3 and int(outs["1"]["launches"]) == 5 * layers + 4
     counts = outs["1"]["counts"]
@@ -317,9 +334,27 @@ def test_fused_and_unfused_layernorm_plans(tmp_path, net, precision):
     print(m)
     tight = precision != "fp8"
     assert m["wdl"] <= (2e-3 if tight else WDL_TOL) and m["prior"] <= (2e-3 if tight else PRIOR_TOL), m
-    w = weights.random_init(card(net), seed=0)
-    boards, legal, _, _ = chess.random_positions(41, 300, 0, 120)
-    ref_p, ref_w = oracle.OracleNetwork(card(net), weights.fp8_weights(w) if precision != "bf16" else w,
-                                        threads=16).evaluate(boards, legal)
-    for flag in ("0", "1"):
-        check(compare(outs[flag]["priors"], outs[flag]["wdl"], ref_p, ref_w, counts), precision)
+    _check_plans_against_oracle(outs, net, precision)
+
+
+@pytest.mark.parametrize("net,precision", [("small", "fp8"), ("small", "bf16"), ("nano", "fp8")])
+def test_normalised_a_plans(tmp_path, net, precision):
+    """QKV and FFN1 normalising x in the GEMM (MRN_GEMM_NORM=1, where the kernel supports the
+    shape: `small` with e4m3 operands) against LayerNorm launches into h (the default). The GEMMs see
+    the same e4m3 A either way (the GEMMs differ only in tile shape: 256-row CTA-pair tiles
+    against 128-row ones), so the outputs agree to accumulation order; elsewhere the switch
+    changes nothing."""
+    outs = _run_plans(tmp_path, net, precision, {"norm0": {"MRN_GEMM_NORM": "0", "MRN_GEMM_LN": "0"},
+                                                 "norm1": {"MRN_GEMM_NORM": "1", "MRN_GEMM_LN": "0"}})
+    layers = card(net).n_layers
+    normalised = net == "small" and precision == "fp8"
+    assert int(outs["norm0"]["launches"]) == 7 * layers + 3
+    assert int(outs["norm1"]["launches"]) == (5 * layers + 4 if normalised else 7 * layers + 3)
+    counts = outs["norm1"]["counts"]
+    m = compare(outs["norm1"]["priors"], outs["norm1"]["wdl"], outs["norm0"]["priors"], outs["norm0"]["wdl"], counts)
+    print(m)
+    if normalised:
+        assert m["wdl"] <= WDL_TOL and m["prior"] <= PRIOR_TOL, m
+    else:
+        assert m["wdl"] == 0 and m["prior"] == 0, m
+    _check_plans_against_oracle(outs, net, precision)

@@ -207,3 +207,116 @@ def test_residual_layernorm_rejects_unsplittable_width(cuda):
                               x.data_ptr(), h.data_ptr(), m, d, k, 1.0, 1e-5, 1.0, ctypes.c_void_p(status.data_ptr()),
                               ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc != 0 and "slice" in lib.mrn_test_last_error().decode()
+
+
+def _layernorm(x, gamma, beta, eps, e4m3, inv_q, out):
+    lib = _lib.load()
+    rows, d = x.shape
+    rc = lib.mrn_test_layernorm(x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), eps, int(e4m3), inv_q,
+                                out.data_ptr(), rows, d, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, lib.mrn_test_last_error().decode()
+    torch.cuda.synchronize()
+
+
+def _run_norm(epi, x, gamma, beta, eps, a_inv_q, b, bias, out, ldo, m, n, k, scale, inv_q):
+    lib = _lib.load()
+    status = torch.zeros(1, dtype=torch.int32, device=x.device)
+    rc = lib.mrn_test_gemm_norm(epi, x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), eps, a_inv_q, b.data_ptr(),
+                                bias.data_ptr(), out.data_ptr(), ldo, m, n, k, scale, inv_q,
+                                ctypes.c_void_p(status.data_ptr()),
+                                ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    if rc != 0:
+        return lib.mrn_test_last_error().decode()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, f"device status {int(status.item())}"
+    return None
+
+
+def _norm_inputs(m, d, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = (torch.randn(m, d, device="cuda", generator=g) * 2.0 + 0.3).half()  # the f16 residual stream
+    gamma = 1.0 + 0.2 * torch.randn(d, device="cuda", generator=g)
+    beta = 0.1 * torch.randn(d, device="cuda", generator=g)
+    return x, gamma, beta
+
+
+@pytest.mark.parametrize("e4m3", [False, True], ids=["bf16", "e4m3"])
+@pytest.mark.parametrize("m,d", [(65 * 7, 512), (65 * 3, 192), (1, 512), (65 * 64, 512), (130, 1024)])
+def test_layernorm_kernel(cuda, e4m3, m, d):
+    """The LayerNorm kernel against torch fp32 LayerNorm of the same f16 rows."""
+    x, gamma, beta = _norm_inputs(m, d, seed=m + d)
+    q, eps = 0.02, 1e-5
+    out = torch.zeros((m, d), device=cuda, dtype=torch.uint8 if e4m3 else torch.bfloat16)
+    _layernorm(x, gamma, beta, eps, e4m3, 1.0 / q, out)
+    ref = torch.nn.functional.layer_norm(x.float(), (d,), gamma, beta, eps)
+    if e4m3:
+        got = out.view(torch.float8_e4m3fn).float() * q
+        _within(got, ref, ref.abs() * 0.0625 + q * 2 ** -6 + 1e-5, "layernorm e4m3")
+    else:
+        _within(out.float(), ref, ref.abs() * 2 ** -8 + 1e-4, "layernorm bf16")
+
+
+# (M, N): QKV and FFN1 of `small` (K = d = 512) with one, two and ragged 256-row blocks, fewer
+# (block, tile) units than CTA pairs, and many blocks per pair (both A buffers reused).
+NORM_SHAPES = [
+    (65 * 7, 1536), (65 * 7, 2048), (1, 256), (256, 256), (257, 512), (65 * 64, 1536), (65 * 131, 2048),
+    (65 * 1024, 1536), (65 * 1024, 2048),
+]
+
+
+@pytest.mark.parametrize("epi", [EPI_BIAS, EPI_GELU_E4M3, EPI_GELU_TANH_E4M3], ids=["bias", "gelu", "gelu_tanh"])
+@pytest.mark.parametrize("m,n", NORM_SHAPES)
+def test_norm_gemm_matches_layernorm_then_gemm(cuda, epi, m, n):
+    """A normalised inside the GEMM: the same e4m3 A as the LayerNorm kernel writes, so the output
+    equals LayerNorm kernel -> GEMM; that A agrees with torch's LayerNorm, and the output with torch
+    fp32 of the GEMM on it."""
+    k, eps, qa = 512, 1e-5, 0.02
+    x, gamma, beta = _norm_inputs(m, k, seed=m + n)
+    g = torch.Generator(device="cuda").manual_seed(n)
+    b8 = (torch.randn(n, k, device=cuda, generator=g) * 0.4).to(torch.float8_e4m3fn)
+    bias = torch.randn(n, device=cuda, generator=g) * 0.1
+    scale, q = qa * 0.05, 0.05
+    e4m3_out = epi != EPI_BIAS
+    odt = torch.uint8 if e4m3_out else torch.bfloat16
+    h = torch.zeros((m, k), device=cuda, dtype=torch.uint8)
+    _layernorm(x, gamma, beta, eps, True, 1.0 / qa, h)
+    want = torch.zeros((m, n), device=cuda, dtype=odt)
+    _run(True, epi, h, b8.view(torch.uint8), bias, want, n, m, n, k, scale=scale, inv_q=1.0 / q)
+    sentinel = 0x55 if e4m3_out else 7.0
+    got = torch.full((m + 64, n), sentinel, device=cuda, dtype=odt)
+    err = _run_norm(epi, x, gamma, beta, eps, 1.0 / qa, b8.view(torch.uint8), bias, got, n, m, n, k, scale, 1.0 / q)
+    assert err is None, err
+    assert bool((got[m:] == sentinel).all()), "rows past M were written"
+    got = got[:m]
+    if e4m3_out:
+        g32, w32 = got.view(torch.float8_e4m3fn).float(), want.view(torch.float8_e4m3fn).float()
+    else:
+        g32, w32 = got.float(), want.float()
+    # Same A, same accumulation per output element: identical up to the MMA's internal order on
+    # the 256-row (CTA pair) against the 128-row tile, at most one output rounding step apart.
+    same = (g32 == w32).float().mean().item()
+    assert same >= 0.999, f"only {same:.4%} of outputs identical to LayerNorm -> GEMM"
+    _within(g32, w32, w32.abs() * (0.0625 if e4m3_out else 2 ** -7) + 1e-6, "norm gemm vs layernorm -> gemm")
+    # A itself: the LayerNorm kernel's e4m3 rows, within one e4m3 step of torch's LayerNorm (a
+    # value on a rounding boundary may round either way, and one flipped code of a large A value
+    # moves a whole output row by a step times |b|, so the GEMM is checked from this A).
+    a_ref = h.view(torch.float8_e4m3fn).float()
+    ln = torch.nn.functional.layer_norm(x.float(), (k,), gamma, beta, eps)
+    _within(a_ref * qa, ln, ln.abs() * 0.0625 + qa * 2 ** -6 + 1e-5, "normalised A vs torch")
+    acc = (a_ref @ b8.float().T) * scale + bias
+    if epi == EPI_BIAS:
+        _within(g32, acc, acc.abs() * 2 ** -7 + 1e-3, "norm gemm vs torch")
+    else:
+        ref = torch.nn.functional.gelu(acc, approximate="tanh" if epi == EPI_GELU_TANH_E4M3 else "none")
+        _within(g32 * q, ref, ref.abs() * 0.0625 + q * 2 ** -6 + 2e-3, "norm gemm vs torch")
+
+
+def test_norm_gemm_rejects_unsupported_shape(cuda):
+    """K = 192 (nano) has no normalised-A instantiation: the plan is refused, nothing is launched."""
+    m, n, k = 65, 576, 192
+    x, gamma, beta = _norm_inputs(m, k, seed=2)
+    b = torch.zeros((n, k), device=cuda, dtype=torch.uint8)
+    bias = torch.zeros(n, device=cuda)
+    out = torch.zeros((m, n), device=cuda, dtype=torch.bfloat16)
+    err = _run_norm(EPI_BIAS, x, gamma, beta, 1e-5, 1.0, b, bias, out, n, m, n, k, 1.0, 1.0)
+    assert err is not None and "gemm+norm" in err
