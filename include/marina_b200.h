@@ -222,6 +222,13 @@ MRN_API int mrn_test_gemm_ln(int fp8, const void* a, const void* b, const float*
 MRN_API int mrn_test_gemm_norm(int epilogue, const void* x, const float* gamma, const float* beta, float eps,
                                float a_inv_q, const void* b, const float* bias, void* out, int ldo, int m, int n,
                                int k, float scale, float inv_q, int* status, void* stream);
+/* The encoder's MLP block in one launch (FFN1 -> GELU -> FFN2 -> residual add; the hidden
+ * [m, ff] tensor never leaves the chip): x[m,d] (f16) += e4m3(GELU(h . w1^T * s1 + b1) * inv_q)
+ * . w2^T * s2 + b2, with e4m3 h [m,d], w1 [ff,d], w2 [d,ff]; `tanh_gelu` selects the tanh form.
+ * d = 512, ff a multiple of 256. */
+MRN_API int mrn_test_mlp(int tanh_gelu, const void* h, const void* w1, const float* b1, const void* w2,
+                         const float* b2, void* x, int m, int d, int ff, float s1, float inv_q, float s2, int* status,
+                         void* stream);
 /* The LayerNorm kernel on its own: out[rows,d] = LN(x) * gamma + beta from f16 x, as bf16, or
  * with `e4m3` as e4m3 codes of the value * inv_q. */
 MRN_API int mrn_test_layernorm(const void* x, const float* gamma, const float* beta, float eps, int e4m3,

@@ -121,6 +121,24 @@ int mrn_test_gemm_norm(int epilogue, const void* x, const float* gamma, const fl
   return run(args, stream);
 }
 
+int mrn_test_mlp(int tanh_gelu, const void* h, const void* w1, const float* b1, const void* w2, const float* b2,
+                 void* x, int m, int d, int ff, float s1, float inv_q, float s2, int* status, void* stream) {
+  if (!prepare()) return fail("gemm_prepare_device failed");
+  mrn::MlpArgs a;
+  a.h = h, a.w1 = w1, a.w2 = w2, a.b1 = b1, a.b2 = b2, a.x = x;
+  a.m = m, a.d = d, a.ff = ff, a.s1 = s1, a.s2 = s2, a.inv_q = inv_q, a.tanh_gelu = tanh_gelu != 0;
+  a.status = status;
+  mrn::MlpPlan plan;
+  char err[256];
+  if (!mrn::mlp_plan(&plan, a, num_sms(), err)) return fail(err);
+  const cudaError_t e = mrn::mlp_launch(plan, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    snprintf(g_test_error, sizeof(g_test_error), "mlp launch: %s", cudaGetErrorString(e));
+    return MRN_ERR_CUDA;
+  }
+  return MRN_OK;
+}
+
 int mrn_test_layernorm(const void* x, const float* gamma, const float* beta, float eps, int e4m3, float inv_q,
                        void* out, int rows, int d, void* stream) {
   const mrn::NormParams np{gamma, beta, eps, out, e4m3 ? mrn::ActType::kE4m3 : mrn::ActType::kBf16, inv_q};

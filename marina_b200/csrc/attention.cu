@@ -150,6 +150,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (lane == 0) raise_error(p.status, abort, kErrTimeoutAttention);
         break;
       }
+      __syncwarp();  // ldmatrix / mma.sync below are .aligned: the whole warp, reconverged
       uint8_t* sq = smem + slot * ITEM;
       const uint32_t aq = smem_u32(sq), ak = aq + MAT, av = aq + 2 * MAT;
       const int pos = item / heads, head = item - pos * heads;

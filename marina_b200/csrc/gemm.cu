@@ -5,6 +5,7 @@
 #include "gemm.cuh"
 #include "gemm.h"
 #include "gemm_ln.cuh"
+#include "gemm_mlp.cuh"
 #include "gemm_norm.cuh"
 #include "tmap.h"
 
@@ -247,6 +248,21 @@ bool plan_norm(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
   return true;
 }
 
+// ---- the fused MLP block (gemm_mlp.cuh)
+template <class Gelu>
+cudaError_t launch_mlp(const MlpPlan& p, const Gelu& gelu, cudaStream_t stream) {
+  const MlpArgs& a = p.args;
+  gemm_mlp_kernel<Gelu><<<p.grid, MlpShape::kThreads, MlpShape::kSmemBytes, stream>>>(
+      p.map_h, p.map_w1, p.map_w2, static_cast<__half*>(a.x), gelu, EpiResidual{a.b2, a.s2}, a.m, a.ff, a.status);
+  return cudaGetLastError();
+}
+
+template <class Gelu>
+cudaError_t prepare_mlp() {
+  return cudaFuncSetAttribute(gemm_mlp_kernel<Gelu>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              MlpShape::kSmemBytes);
+}
+
 bool plan_ln(GemmPlan* plan, const GemmArgs& args, char* err) {
   const int eb = args.fp8 ? 1 : 2;
   plan->bn = gemm_ln_pick_bn(args.n);
@@ -295,6 +311,37 @@ bool gemm_norm_supported(const GemmArgs& a) {
          (a.epi == Epilogue::kBias || a.epi == Epilogue::kGeluE4m3 || a.epi == Epilogue::kGeluTanhE4m3) && a.norm_x &&
          a.gamma && a.beta && a.bias && a.out && aligned(a.norm_x) && aligned(a.gamma) && aligned(a.beta) &&
          aligned(a.bias) && aligned(a.out);
+}
+
+bool mlp_supported(const MlpArgs& a) {
+  auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  return a.m > 0 && a.d == kMlpD && a.ff >= 512 && a.ff % 256 == 0 && a.h && a.w1 && a.w2 && a.b1 && a.b2 && a.x &&
+         aligned(a.h) && aligned(a.w1) && aligned(a.w2) && aligned(a.b1) && aligned(a.b2) && aligned(a.x);
+}
+
+bool mlp_plan(MlpPlan* plan, const MlpArgs& a, int num_sms, char* err) {
+  if (!mlp_supported(a)) {
+    snprintf(err, 256, "mlp: needs d = %d, ff a multiple of 256 (>= 512), aligned buffers (M=%d d=%d ff=%d)", kMlpD,
+             a.m, a.d, a.ff);
+    return false;
+  }
+  plan->args = a;
+  if (!make_kmajor_map(&plan->map_h, a.h, 1, a.m, a.d, kTileM) ||
+      !make_kmajor_map(&plan->map_w1, a.w1, 1, a.ff, a.d, MlpShape::kChunk) ||
+      !make_kmajor_map(&plan->map_w2, a.w2, 1, a.d, a.ff, MlpShape::kOutCols)) {
+    snprintf(err, 256, "mlp: cuTensorMapEncodeTiled failed (M=%d d=%d ff=%d)", a.m, a.d, a.ff);
+    return false;
+  }
+  const int tiles = (a.m + kTileM - 1) / kTileM;
+  const int clusters = num_sms / 2;
+  plan->grid = 2 * (tiles < clusters ? tiles : clusters);
+  return true;
+}
+
+cudaError_t mlp_launch(const MlpPlan& p, cudaStream_t stream) {
+  const MlpArgs& a = p.args;
+  if (a.tanh_gelu) return launch_mlp(p, EpiGeluTanh<true>{a.b1, a.s1, a.inv_q}, stream);
+  return launch_mlp(p, EpiGelu<true>{a.b1, a.s1, a.inv_q}, stream);
 }
 
 int gemm_pick_bn(int n) {
@@ -403,6 +450,8 @@ cudaError_t gemm_prepare_device() {
   if ((e = prepare_ln<128>()) != cudaSuccess) return e;
   if ((e = prepare_ln<96>()) != cudaSuccess) return e;
   if ((e = prepare_ln<64>()) != cudaSuccess) return e;
+  if ((e = prepare_mlp<EpiGelu<true>>()) != cudaSuccess) return e;
+  if ((e = prepare_mlp<EpiGeluTanh<true>>()) != cudaSuccess) return e;
   if ((e = prepare_norm<EpiBiasBf16>()) != cudaSuccess) return e;
   if ((e = prepare_norm<EpiGelu<true>>()) != cudaSuccess) return e;
   if ((e = prepare_norm<EpiGeluTanh<true>>()) != cudaSuccess) return e;

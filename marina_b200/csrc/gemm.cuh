@@ -179,6 +179,13 @@ struct EpiBiasBf16 {
   }
 };
 
+// The 32 bias values of an epilogue chunk starting at column `col`, as 8 vectors (loaded ahead of
+// the accumulator where a kernel has the registers to spare).
+__device__ __forceinline__ void load_bias32(const float* bias, int col, float4 (&b)[8]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) b[k] = __ldg(reinterpret_cast<const float4*>(bias + col) + k);
+}
+
 // out = GELU(acc * scale + bias) as bf16, or as e4m3 codes of value * inv_q (saturating).
 // The GELU is the bulk of the epilogue's arithmetic, so it gets 16 warps.
 template <bool E4M3>
@@ -190,6 +197,12 @@ struct EpiGelu {
   float scale;
   float inv_q;
   __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[kOutBytes * 2]) const {
+    float4 b[8];
+    load_bias32(bias, col, b);
+    pack_with(b, v, o);
+  }
+  __device__ __forceinline__ void pack_with(const float4 (&b)[8], const float (&v)[32],
+                                            uint4 (&o)[kOutBytes * 2]) const {
     const float2 s2 = make_float2(scale, scale);
     if constexpr (E4M3) {
       const __half2 iq = __float2half2_rn(inv_q);
@@ -198,9 +211,9 @@ struct EpiGelu {
         __nv_fp8x2_storage_t q[8];
 #pragma unroll
         for (int j = 0; j < 8; j += 2) {
-          const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c + 2 * j));
-          const float2 x0 = fma2(make_float2(v[c + 2 * j], v[c + 2 * j + 1]), s2, make_float2(b.x, b.y));
-          const float2 x1 = fma2(make_float2(v[c + 2 * j + 2], v[c + 2 * j + 3]), s2, make_float2(b.z, b.w));
+          const float4 bb = b[(c + 2 * j) / 4];
+          const float2 x0 = fma2(make_float2(v[c + 2 * j], v[c + 2 * j + 1]), s2, make_float2(bb.x, bb.y));
+          const float2 x1 = fma2(make_float2(v[c + 2 * j + 2], v[c + 2 * j + 3]), s2, make_float2(bb.z, bb.w));
           const __half2 y0 = __hmul2(gelu_h2(f32x2_to_h2_sat(x0)), iq);
           const __half2 y1 = __hmul2(gelu_h2(f32x2_to_h2_sat(x1)), iq);
           q[j] = __nv_cvt_halfraw2_to_fp8x2(y0, __NV_SATFINITE, __NV_E4M3);
@@ -211,9 +224,9 @@ struct EpiGelu {
     } else {
 #pragma unroll
       for (int c = 0; c < 32; c += 4) {
-        const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c));
-        const float2 y0 = gelu2(fma2(make_float2(v[c], v[c + 1]), s2, make_float2(b.x, b.y)));
-        const float2 y1 = gelu2(fma2(make_float2(v[c + 2], v[c + 3]), s2, make_float2(b.z, b.w)));
+        const float4 bb = b[c / 4];
+        const float2 y0 = gelu2(fma2(make_float2(v[c], v[c + 1]), s2, make_float2(bb.x, bb.y)));
+        const float2 y1 = gelu2(fma2(make_float2(v[c + 2], v[c + 3]), s2, make_float2(bb.z, bb.w)));
         __nv_bfloat162 p[2] = {__floats2bfloat162_rn(y0.x, y0.y), __floats2bfloat162_rn(y1.x, y1.y)};
         reinterpret_cast<uint2*>(o)[c / 4] = *reinterpret_cast<const uint2*>(p);
       }
@@ -246,12 +259,18 @@ struct EpiGeluTanh {
   float scale;
   float inv_q;
   __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[kOutBytes * 2]) const {
+    float4 b[8];
+    load_bias32(bias, col, b);
+    pack_with(b, v, o);
+  }
+  __device__ __forceinline__ void pack_with(const float4 (&b)[8], const float (&v)[32],
+                                            uint4 (&o)[kOutBytes * 2]) const {
     const float2 s2 = make_float2(scale, scale);
 #pragma unroll
     for (int c = 0; c < 32; c += 4) {
-      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col + c));
-      const float2 x0 = fma2(make_float2(v[c], v[c + 1]), s2, make_float2(b.x, b.y));
-      const float2 x1 = fma2(make_float2(v[c + 2], v[c + 3]), s2, make_float2(b.z, b.w));
+      const float4 bb = b[c / 4];
+      const float2 x0 = fma2(make_float2(v[c], v[c + 1]), s2, make_float2(bb.x, bb.y));
+      const float2 x1 = fma2(make_float2(v[c + 2], v[c + 3]), s2, make_float2(bb.z, bb.w));
       const float y0 = gelu_tanh(x0.x), y1 = gelu_tanh(x0.y), y2 = gelu_tanh(x1.x), y3 = gelu_tanh(x1.y);
       if constexpr (E4M3) {
         __nv_fp8x2_storage_t q[2] = {

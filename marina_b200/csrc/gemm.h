@@ -77,6 +77,32 @@ cudaError_t gemm_prepare_device();
 
 cudaError_t gemm_launch(const GemmPlan& plan, cudaStream_t stream);
 
+// The encoder's MLP block in one launch (gemm_mlp.cuh): x += e4m3(GELU(h · w1^T · s1 + b1) · inv_q)
+// · w2^T · s2 + b2, e4m3 operands, d = 512, ff a multiple of 256; the [M, ff] hidden tensor stays
+// on chip.
+struct MlpArgs {
+  const void* h = nullptr;    // [M, d] e4m3
+  const void* w1 = nullptr;   // [ff, d] e4m3
+  const void* w2 = nullptr;   // [d, ff] e4m3
+  const float* b1 = nullptr;  // [ff]
+  const float* b2 = nullptr;  // [d]
+  void* x = nullptr;          // [M, d] f16 residual stream
+  int m = 0, d = 0, ff = 0;
+  float s1 = 1.f, s2 = 1.f, inv_q = 1.f;
+  bool tanh_gelu = false;     // the card's tanh-form GELU
+  int* status = nullptr;
+};
+
+struct MlpPlan {
+  CUtensorMap map_h, map_w1, map_w2;
+  MlpArgs args;
+  int grid = 0;
+};
+
+bool mlp_supported(const MlpArgs& args);
+bool mlp_plan(MlpPlan* plan, const MlpArgs& args, int num_sms, char* err);
+cudaError_t mlp_launch(const MlpPlan& plan, cudaStream_t stream);
+
 // Algorithmic FLOPs of one launch (2·M·N·K).
 inline double gemm_flops(const GemmArgs& a) { return 2.0 * a.m * static_cast<double>(a.n) * a.k; }
 

@@ -23,7 +23,7 @@ enum DeviceError : int {
   kErrTimeoutMma = 2,
   kErrTimeoutEpilogue = 3,
   kErrTimeoutDrain = 4,
-  kErrTimeoutExchange = 5,  // a row-statistics exchange between the CTAs of a cluster
+  kErrTimeoutExchange = 5,  // an exchange between the CTAs of a cluster (row statistics, hidden chunks)
   // 6: attention.cu's producer/consumer handshake
   kErrTimeoutNorm = 7,      // a norm warp of the normalised-A GEMM waiting for its A buffer
 };
@@ -205,9 +205,12 @@ __device__ __forceinline__ void mma_e4m3(uint32_t d, uint64_t a, uint64_t b, uin
 
 // 32 consecutive 32-bit TMEM columns of this thread's lane (32x32b shape: warp w reads
 // lanes 32*(w%4) .. 32*(w%4)+31, one lane per thread). The wait is inside the same asm
-// statement so no use of the registers can be scheduled before the data has landed.
+// statement so no use of the registers can be scheduled before the data has landed. The load
+// is a .sync.aligned warp instruction: the whole warp must execute it together, so the warp is
+// reconverged first (callers reach it after per-lane waits and lane-0-only or per-row branches).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
+  __syncwarp();
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -226,6 +229,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // The same for 16 consecutive columns.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
+  __syncwarp();
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
@@ -372,6 +376,42 @@ __device__ __forceinline__ void mma_pair_e4m3(uint32_t d, uint64_t a, uint64_t b
       "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(d),
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u)
       : "memory");
+}
+
+// Arrive on the mbarrier at this shared-memory offset in every CTA of `cta_mask` once the
+// (single-CTA) MMAs issued so far by this thread have completed.
+__device__ __forceinline__ void tc_commit_mc(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+
+// Copy `bytes` (a multiple of 16) of this CTA's shared memory to another CTA of the cluster
+// (`dst_cluster`, `bar_cluster`: addresses from map_to_rank); completion is counted as
+// transaction bytes on that CTA's mbarrier.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, const void* src, uint32_t bytes,
+                                                  uint32_t bar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst_cluster),
+               "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
+               : "memory");
+}
+
+// Arrive on an mbarrier of another CTA of the cluster and add `bytes` to its expected
+// transaction count (address from map_to_rank).
+__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t cluster_addr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_addr),
+               "r"(bytes)
+               : "memory");
+}
+
+// Pull a 2-D tile of a tensor map into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
 }
 
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA with 128-byte

@@ -248,6 +248,28 @@ bool ln_fusion_enabled() {
   return on;
 }
 
+bool mlp_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("MRN_MLP");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
+bool mlp_args(const GemmArgs& f1, const GemmArgs& f2, MlpArgs* out) {
+  if (!f1.fp8 || !f2.fp8 || f1.norm_x || f2.epi != Epilogue::kResidual ||
+      (f1.epi != Epilogue::kGeluE4m3 && f1.epi != Epilogue::kGeluTanhE4m3))
+    return false;
+  MlpArgs a;
+  a.h = f1.a, a.w1 = f1.b, a.w2 = f2.b, a.b1 = f1.bias, a.b2 = f2.bias, a.x = f2.out;
+  a.m = f1.m, a.d = f1.k, a.ff = f1.n, a.s1 = f1.scale, a.s2 = f2.scale, a.inv_q = f1.inv_q;
+  a.tanh_gelu = f1.epi == Epilogue::kGeluTanhE4m3;
+  a.status = f1.status;
+  if (f2.k != a.ff || f2.n != a.d || f2.ldo != a.d || f1.ldo != a.ff || !mlp_supported(a)) return false;
+  *out = a;
+  return true;
+}
+
 bool norm_a_enabled() {
   static const bool on = [] {
     const char* e = getenv("MRN_GEMM_NORM");
@@ -297,7 +319,7 @@ bool qkv_normalises(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bo
   return g.norm_x != nullptr;
 }
 
-void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool fuse, bool norm,
+void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool fuse, bool norm, bool mlp,
                      GemmArgs (&g)[4]) {
   const int d = c->d, ff = c->dff;
   const bool fp8 = c->precision == MRN_PRECISION_FP8;
@@ -310,7 +332,7 @@ void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, b
   g[2].epi = fp8 ? (tanh_form ? Epilogue::kGeluTanhE4m3 : Epilogue::kGeluE4m3)
                  : (tanh_form ? Epilogue::kGeluTanhBf16 : Epilogue::kGeluBf16);
   g[2].out = b.ff, g[2].ldo = ff, g[2].bias = D.b_1, g[2].scale = gemm_scale(c, D, 2), g[2].inv_q = 1.f / D.as[3];
-  if (norm) try_norm(g[2], b, D.n2g, D.n2b, D.as[2]);
+  if (norm && !mlp) try_norm(g[2], b, D.n2g, D.n2b, D.as[2]);
   // out-proj: attn -> x += (then h = norm2(x), unless FFN1 normalises x itself)
   g[1].a = b.attn, g[1].b = D.w_o, g[1].n = d, g[1].k = d, g[1].epi = Epilogue::kResidual, g[1].out = b.x;
   g[1].ldo = d, g[1].bias = D.b_o, g[1].scale = gemm_scale(c, D, 1);
@@ -321,7 +343,7 @@ void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, b
   // FFN2: ff -> x += (then h = norm1 of the next layer, unless its QKV normalises x itself)
   g[3].a = b.ff, g[3].b = D.w_2, g[3].n = d, g[3].k = ff, g[3].epi = Epilogue::kResidual, g[3].out = b.x;
   g[3].ldo = d, g[3].bias = D.b_2, g[3].scale = gemm_scale(c, D, 3);
-  if (fuse && l + 1 < c->layers && !qkv_normalises(c, l + 1, rows, b, norm)) {
+  if (fuse && !mlp && l + 1 < c->layers && !qkv_normalises(c, l + 1, rows, b, norm)) {
     const DevLayer& N = c->dl[l + 1];
     g[3].epi = Epilogue::kResidualLn, g[3].gamma = N.n1g, g[3].beta = N.n1b, g[3].ln_out = b.h;
     g[3].ln_inv_q = 1.f / N.as[0];
@@ -351,9 +373,25 @@ int make_plans(mrn_ctx* c, Bucket& b) {
   const bool fuse = mrn::ln_fusion_enabled(), norm = mrn::norm_a_enabled();
   b.ln_launch.assign(2 * L, 0);
   b.embed_norm = !mrn::qkv_normalises(c, 0, M, bufs, norm);
+  // The fused MLP where the switch is on and every layer supports it.
+  bool mlp = mrn::mlp_enabled();
+  for (int l = 0; l < L && mlp; ++l) {
+    GemmArgs g[4];
+    mrn::MlpArgs a;
+    mrn::layer_gemm_args(c, l, M, bufs, fuse, norm, true, g);
+    mlp = mrn::mlp_args(g[2], g[3], &a);
+  }
+  b.mlp.clear();
   for (int l = 0; l < L; ++l) {
     GemmArgs g[4];
-    mrn::layer_gemm_args(c, l, M, bufs, fuse, norm, g);
+    mrn::layer_gemm_args(c, l, M, bufs, fuse, norm, mlp, g);
+    if (mlp) {
+      mrn::MlpArgs a;
+      mrn::MlpPlan mp;
+      mrn::mlp_args(g[2], g[3], &a);
+      if (!mrn::mlp_plan(&mp, a, c->num_sms, err)) return c->fail(MRN_ERR_UNSUPPORTED, "layer %d: %s", l, err);
+      b.mlp.push_back(mp);
+    }
     bool ln_in_epilogue[2] = {false, false};
     for (int i = 0; i < 4; ++i) {
       GemmPlan p;
@@ -417,8 +455,12 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
       done();
     }
     mark(MRN_PROFILE_GEMM);
-    CK(mrn::gemm_launch(plans[2], s));
-    CK(mrn::gemm_launch(plans[3], s));
+    if (b.mlp.empty()) {
+      CK(mrn::gemm_launch(plans[2], s));
+      CK(mrn::gemm_launch(plans[3], s));
+    } else {
+      CK(mrn::mlp_launch(b.mlp[l], s));
+    }
     done();
     if (b.ln_launch[2 * l + 1]) {
       mark(MRN_PROFILE_LAYERNORM);
@@ -442,10 +484,13 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
   return MRN_OK;
 }
 
-// Embedding, 5 per layer (QKV, attention, out-proj, FFN1, FFN2), a LayerNorm launch wherever no GEMM
-// computes that norm (norm2, and norm1 of every layer but the first), 3 for the heads.
+// Per layer: QKV, attention, out-proj, then FFN1 + FFN2 or the fused MLP.
+int layer_launches(const Bucket& b) { return b.mlp.empty() ? 5 : 4; }
+
+// Embedding, the layers' launches, a LayerNorm launch wherever no GEMM computes that norm (norm2,
+// and norm1 of every layer but the first), 3 for the heads.
 int launches_per_forward(const mrn_ctx* c, const Bucket& b) {
-  int n = 1 + 5 * c->layers + 3;
+  int n = 1 + layer_launches(b) * c->layers + 3;
   for (uint8_t launch : b.ln_launch) n += launch;
   return n;
 }
@@ -764,10 +809,10 @@ MRN_API int mrn_profile(mrn_ctx* c, int n, const uint8_t* d_boards, const int32_
   }
   if (rc) return rc;
   for (size_t i = 0; i < b->plans.size(); ++i) flops[MRN_PROFILE_GEMM] += mrn::gemm_flops(b->plans[i].args);
-  launches[MRN_PROFILE_GEMM] = static_cast<int>(b->plans.size());
+  launches[MRN_PROFILE_GEMM] = static_cast<int>(b->plans.size()) - (b->mlp.empty() ? 0 : c->layers);
   launches[MRN_PROFILE_EMBED] = 1;
   launches[MRN_PROFILE_ATTENTION] = c->layers;
-  launches[MRN_PROFILE_LAYERNORM] = launches_per_forward(c, *b) - (1 + 5 * c->layers + 3);
+  launches[MRN_PROFILE_LAYERNORM] = launches_per_forward(c, *b) - (1 + layer_launches(*b) * c->layers + 3);
   launches[MRN_PROFILE_HEADS] = 2;
   flops[MRN_PROFILE_ATTENTION] = 4.0 * P * static_cast<double>(c->t) * c->t * c->d * c->layers;
   CK(cudaMemcpyAsync(d_priors, c->priors, static_cast<size_t>(n) * MRN_MAX_LEGAL * 4, cudaMemcpyDeviceToDevice, s));

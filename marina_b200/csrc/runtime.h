@@ -37,6 +37,7 @@ struct Bucket {
   // (gemm_norm.cuh) or in the residual GEMM's epilogue (gemm_ln.cuh).
   std::vector<uint8_t> ln_launch;
   bool embed_norm = true;  // the embedding kernel writes layer 0's norm1 (its QKV does not normalise A)
+  std::vector<MlpPlan> mlp;  // per layer when FFN1 + FFN2 run as one fused MLP launch (else empty)
   cudaGraphExec_t graph = nullptr;
 };
 
@@ -133,8 +134,15 @@ namespace mrn {
 // FFN1 compute norm1 / norm2 of x themselves where the normalised-A kernel supports the shape.
 // With `fuse`, out-proj carries norm2 and FFN2 (all layers but the last) the next layer's norm1 as
 // the fused residual + LayerNorm epilogue, unless the consuming GEMM normalises A itself.
-void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool fuse, bool norm,
+// With `mlp`, FFN1 and FFN2 are planned for the fused MLP kernel (mlp_args): FFN1 reads h and FFN2
+// carries no LayerNorm.
+void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool fuse, bool norm, bool mlp,
                      GemmArgs (&g)[4]);
+// The fused MLP of a layer from its FFN1 and FFN2 arguments; false where the kernel does not
+// support the layer (not e4m3, d != 512, ...).
+bool mlp_args(const GemmArgs& ffn1, const GemmArgs& ffn2, MlpArgs* out);
+// Whether FFN1 + FFN2 run as one fused launch (environment MRN_MLP=1; off by default).
+bool mlp_enabled();
 // Whether layer l's QKV GEMM computes norm1 itself (under the same `norm` setting).
 bool qkv_normalises(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool norm);
 // Whether plans use the fused residual + LayerNorm epilogue (environment MRN_GEMM_LN=1; off by default).

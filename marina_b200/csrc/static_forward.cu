@@ -141,6 +141,13 @@ int forward(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, floa
   const mrn::DevLayer& D0 = c->dl[0];
   const mrn::LayerBuffers bufs{h, qkv, attn, ff, x};
   const bool fuse = mrn::ln_fusion_enabled(), norm = mrn::norm_a_enabled();
+  bool mlp = mrn::mlp_enabled();
+  for (int l = 0; l < c->layers && mlp; ++l) {
+    mrn::GemmArgs g[4];
+    mrn::MlpArgs a;
+    mrn::layer_gemm_args(c, l, R, bufs, fuse, norm, true, g);
+    mlp = mrn::mlp_args(g[2], g[3], &a);
+  }
   CKS(mrn::launch_embed_ln(
       mrn::EmbedParams{boards, c->piece, c->square, c->state, c->cast_w, c->cast_b, c->ep, x, c->t, c->square_start},
       mrn::NormParams{D0.n1g, D0.n1b, c->eps, mrn::qkv_normalises(c, 0, R, bufs, norm) ? nullptr : h, act,
@@ -149,14 +156,24 @@ int forward(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, floa
   for (int l = 0; l < c->layers; ++l) {
     const mrn::DevLayer& D = c->dl[l];
     mrn::GemmArgs g[4];
-    mrn::layer_gemm_args(c, l, R, bufs, fuse, norm, g);
+    mrn::layer_gemm_args(c, l, R, bufs, fuse, norm, mlp, g);
     if ((rc = gemm(c, g[0], s))) return rc;
     CKS(mrn::launch_attention(mrn::AttentionParams{qkv, attn, act, 1.f / D.as[1], c->t, d, c->heads, c->status}, n,
                               d / c->heads, s));
     if ((rc = residual(c, l, 0, g[1], bufs, !g[2].norm_x, s))) return rc;
-    if ((rc = gemm(c, g[2], s))) return rc;
     const bool need_h = l + 1 < c->layers && !mrn::qkv_normalises(c, l + 1, R, bufs, norm);
-    if ((rc = residual(c, l, 1, g[3], bufs, need_h, s))) return rc;
+    if (mlp) {
+      mrn::MlpArgs a;
+      mrn::MlpPlan mp;
+      char err[256];
+      mrn::mlp_args(g[2], g[3], &a);
+      if (!mrn::mlp_plan(&mp, a, c->num_sms, err)) return c->fail(MRN_ERR_UNSUPPORTED, "%s", err);
+      CKS(mrn::mlp_launch(mp, s));
+      if (need_h) CKS(mrn::launch_site_layernorm(c, l, 1, bufs, R, s));
+    } else {
+      if ((rc = gemm(c, g[2], s))) return rc;
+      if ((rc = residual(c, l, 1, g[3], bufs, need_h, s))) return rc;
+    }
   }
   mrn::HeadsParams hp;
   hp.x = x, hp.final_g = c->fn_g, hp.final_b = c->fn_b, hp.policy_g = c->pn_g, hp.policy_b = c->pn_b;

@@ -358,3 +358,25 @@ def test_normalised_a_plans(tmp_path, net, precision):
     else:
         assert m["wdl"] == 0 and m["prior"] == 0, m
     _check_plans_against_oracle(outs, net, precision)
+
+
+@pytest.mark.parametrize("net,precision", [("small", "fp8"), ("small", "bf16"), ("nano", "fp8")])
+def test_fused_mlp_plans(tmp_path, net, precision):
+    """FFN1 + FFN2 as one fused MLP launch per layer (MRN_MLP=1, where the kernel supports the
+    layer: `small` with e4m3 operands) against the two GEMM launches (the default). The hidden
+    values and the FFN2 accumulation order are the same, so the outputs agree to rounding; elsewhere
+    the switch changes nothing."""
+    outs = _run_plans(tmp_path, net, precision, {"mlp0": {"MRN_MLP": "0", "MRN_GEMM_LN": "0"},
+                                                 "mlp1": {"MRN_MLP": "1", "MRN_GEMM_LN": "0"}})
+    layers = card(net).n_layers
+    fused = net == "small" and precision == "fp8"
+    assert int(outs["mlp0"]["launches"]) == 7 * layers + 3
+    assert int(outs["mlp1"]["launches"]) == (6 * layers + 3 if fused else 7 * layers + 3)
+    counts = outs["mlp1"]["counts"]
+    m = compare(outs["mlp1"]["priors"], outs["mlp1"]["wdl"], outs["mlp0"]["priors"], outs["mlp0"]["wdl"], counts)
+    print(m)
+    if fused:
+        assert m["wdl"] <= WDL_TOL and m["prior"] <= PRIOR_TOL, m
+    else:
+        assert m["wdl"] == 0 and m["prior"] == 0, m
+    _check_plans_against_oracle(outs, net, precision)

@@ -320,3 +320,70 @@ def test_norm_gemm_rejects_unsupported_shape(cuda):
     out = torch.zeros((m, n), device=cuda, dtype=torch.bfloat16)
     err = _run_norm(EPI_BIAS, x, gamma, beta, 1e-5, 1.0, b, bias, out, n, m, n, k, 1.0, 1.0)
     assert err is not None and "gemm+norm" in err
+
+
+def _run_mlp(tanh, h, w1, b1, w2, b2, x, m, d, ff, s1, inv_q, s2):
+    lib = _lib.load()
+    status = torch.zeros(1, dtype=torch.int32, device=h.device)
+    rc = lib.mrn_test_mlp(int(tanh), h.data_ptr(), w1.data_ptr(), b1.data_ptr(), w2.data_ptr(), b2.data_ptr(),
+                          x.data_ptr(), m, d, ff, s1, inv_q, s2, ctypes.c_void_p(status.data_ptr()),
+                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    if rc != 0:
+        return lib.mrn_test_last_error().decode()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, f"device status {int(status.item())}"
+    return None
+
+
+# (M, ff) with d = 512: one row, ragged and exact 128-row tiles, fewer tiles than CTA pairs, many
+# tiles per pair (all hidden-chunk slots reused), and the smallest and a middle ff.
+MLP_SHAPES = [(1, 2048), (65 * 3, 2048), (128, 2048), (129, 512), (65 * 64, 2048), (65 * 1024, 2048),
+              (65 * 37, 1024), (65 * 512, 512)]
+
+
+@pytest.mark.parametrize("tanh", [False, True], ids=["erf", "tanh"])
+@pytest.mark.parametrize("m,ff", MLP_SHAPES)
+def test_fused_mlp_matches_two_gemms(cuda, tanh, m, ff):
+    """FFN1 -> GELU -> FFN2 -> residual in one kernel against the two GEMM launches it replaces
+    (the same e4m3 hidden values and the same accumulation order, so the same x), and against
+    torch fp32 of the same op on the hidden tensor the first GEMM writes."""
+    d = 512
+    g = torch.Generator(device="cuda").manual_seed(m + ff + int(tanh))
+    h = (torch.randn(m, d, device=cuda, generator=g) * 2.0).to(torch.float8_e4m3fn)
+    w1 = (torch.randn(ff, d, device=cuda, generator=g) * 0.5).to(torch.float8_e4m3fn)
+    w2 = (torch.randn(d, ff, device=cuda, generator=g) * 0.5).to(torch.float8_e4m3fn)
+    b1 = torch.randn(ff, device=cuda, generator=g) * 0.1
+    b2 = torch.randn(d, device=cuda, generator=g) * 0.1
+    s1, q, s2 = 0.01, 0.02, 0.0005
+    x0 = torch.randn(m, d, device=cuda, generator=g).half()
+    # the two launches it replaces
+    f = torch.zeros((m, ff), device=cuda, dtype=torch.uint8)
+    _run(True, EPI_GELU_TANH_E4M3 if tanh else EPI_GELU_E4M3, h.view(torch.uint8), w1.view(torch.uint8), b1, f, ff,
+         m, ff, d, scale=s1, inv_q=1.0 / q)
+    want = x0.clone()
+    _run(True, EPI_RESIDUAL, f, w2.view(torch.uint8), b2, want, d, m, d, ff, scale=s2)
+    # the fused kernel; rows past m stay
+    x = torch.cat([x0, torch.full((64, d), 3.0, device=cuda, dtype=torch.float16)])
+    err = _run_mlp(tanh, h.view(torch.uint8), w1.view(torch.uint8), b1, w2.view(torch.uint8), b2, x, m, d, ff, s1,
+                   1.0 / q, s2)
+    assert err is None, err
+    assert bool((x[m:] == 3.0).all()), "rows past M were written"
+    got, ref = x[:m].float(), want.float()
+    same = (got == ref).float().mean().item()
+    assert same >= 0.999, f"only {same:.4%} of x identical to the two-launch path"
+    delta = ref - x0.float()
+    _within(got, ref, (ref.abs() + delta.abs()) * 2 ** -10 + 2 ** -14, "fused mlp vs two launches")
+    # torch fp32 from the hidden tensor the first launch wrote
+    ref32 = x0.float() + (f.view(torch.float8_e4m3fn).float() @ w2.float().T) * s2 + b2
+    d32 = ref32 - x0.float()
+    _within(got, ref32, (ref32.abs() + d32.abs()) * 2 ** -10 + 2 ** -14, "fused mlp vs torch")
+
+
+def test_fused_mlp_rejects_unsupported_shape(cuda):
+    """d = 192 (nano) has no fused instantiation: the plan is refused, nothing is launched."""
+    m, d, ff = 65, 192, 768
+    z8 = torch.zeros((ff, d), device=cuda, dtype=torch.uint8)
+    b = torch.zeros(ff, device=cuda)
+    x = torch.zeros((m, d), device=cuda, dtype=torch.float16)
+    err = _run_mlp(False, z8, z8, b, z8, b, x, m, d, ff, 1.0, 1.0, 1.0)
+    assert err is not None and "mlp" in err
