@@ -229,6 +229,11 @@ MRN_API int mrn_test_gemm_norm(int epilogue, const void* x, const float* gamma, 
 MRN_API int mrn_test_mlp(int tanh_gelu, const void* h, const void* w1, const float* b1, const void* w2,
                          const float* b2, void* x, int m, int d, int ff, float s1, float inv_q, float s2, int* status,
                          void* stream);
+/* The attention kernel on its own: per (position, head), softmax(Q K^T / sqrt(hd)) V over the
+ * position's 65 tokens from bf16 qkv [positions*65, 3d] (Q | K | V, head h at columns h*hd) into
+ * out [positions*65, d], bf16, or with `e4m3` as e4m3 codes of the value * inv_q. */
+MRN_API int mrn_test_attention(const void* qkv, void* out, int positions, int d, int heads, int e4m3, float inv_q,
+                               int* status, void* stream);
 /* The LayerNorm kernel on its own: out[rows,d] = LN(x) * gamma + beta from f16 x, as bf16, or
  * with `e4m3` as e4m3 codes of the value * inv_q. */
 MRN_API int mrn_test_layernorm(const void* x, const float* gamma, const float* beta, float eps, int e4m3,

@@ -30,7 +30,7 @@ PROFILE_SLOTS = ("embed", "layernorm", "gemm", "attention", "heads")
 EXPORTS = (
     "mrn_create", "mrn_evaluate", "mrn_logits", "mrn_evaluate_device", "mrn_status_word",
     "mrn_profile", "mrn_launches_per_forward", "mrn_describe", "mrn_last_error", "mrn_destroy",
-    "mrn_test_gemm", "mrn_test_gemm_ln", "mrn_test_gemm_norm", "mrn_test_mlp", "mrn_test_layernorm",
+    "mrn_test_gemm", "mrn_test_gemm_ln", "mrn_test_gemm_norm", "mrn_test_mlp", "mrn_test_attention", "mrn_test_layernorm",
     "mrn_test_last_error",
     "mrn_evaluate_device_static",
 )
@@ -95,6 +95,7 @@ def load() -> ctypes.CDLL:
                                        c_void_p, c_int, c_int, c_int, c_int, c_float, c_float, c_void_p, c_void_p]),
         "mrn_test_mlp": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                  c_int, c_float, c_float, c_float, c_void_p, c_void_p]),
+        "mrn_test_attention": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_void_p, c_void_p]),
         "mrn_test_layernorm": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_int, c_float, c_void_p, c_int, c_int,
                                        c_void_p]),
         "mrn_test_last_error": (c_char_p, []),

@@ -139,6 +139,23 @@ int mrn_test_mlp(int tanh_gelu, const void* h, const void* w1, const float* b1, 
   return MRN_OK;
 }
 
+int mrn_test_attention(const void* qkv, void* out, int positions, int d, int heads, int e4m3, float inv_q, int* status,
+                       void* stream) {
+  static bool prepared = false;
+  if (!prepared) {
+    if (mrn::prepare_attention() != cudaSuccess) return fail("prepare_attention failed");
+    prepared = true;
+  }
+  if (heads <= 0 || d % heads != 0) return fail("attention: d must be a multiple of heads");
+  const mrn::AttentionParams ap{qkv, out, e4m3 ? mrn::ActType::kE4m3 : mrn::ActType::kBf16, inv_q, 65, d, heads, status};
+  const cudaError_t e = mrn::launch_attention(ap, positions, d / heads, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    snprintf(g_test_error, sizeof(g_test_error), "attention launch: %s", cudaGetErrorString(e));
+    return MRN_ERR_CUDA;
+  }
+  return MRN_OK;
+}
+
 int mrn_test_layernorm(const void* x, const float* gamma, const float* beta, float eps, int e4m3, float inv_q,
                        void* out, int rows, int d, void* stream) {
   const mrn::NormParams np{gamma, beta, eps, out, e4m3 ? mrn::ActType::kE4m3 : mrn::ActType::kBf16, inv_q};
