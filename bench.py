@@ -56,6 +56,8 @@ def parse_args():
     ap.add_argument("--precision", choices=["fp8", "fp8w", "bf16"], default="fp8")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-fp8-peak", action="store_true",
+                    help="skip measuring the e4m3 tensor peak (the roofline then uses 2x the bf16 figure)")
     ap.add_argument("--mode", choices=["step", "sweep", "puct", "wholebox", "gemm"], default="step",
                     help="step: the contract's JSON line; sweep: configs[2] latency/throughput per batch size; "
                          "puct: configs[3] nodes/s of the batched PUCT search; wholebox: configs[4] 1M positions; "
@@ -216,6 +218,46 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def measure_fp8_peak(dev, seconds: float = 1.5) -> float | None:
+    """Sustained dense e4m3 throughput of this GPU in TFLOP/s: cuBLASLt (torch._scaled_mm) on
+    8192^3 e4m3 x e4m3 -> bf16, back to back for `seconds`, timed with CUDA events over the last
+    two thirds (after the clocks have settled at the power cap). The roofline denominator for the
+    FP8 GEMMs, which MEASURED_PEAKS.json does not carry; None if the probe cannot run."""
+    import torch
+
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+        b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+        one = torch.tensor(1.0, device=dev)
+
+        def mm():
+            return torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+
+        for _ in range(3):
+            mm()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            mm()
+        e1.record()
+        torch.cuda.synchronize()
+        per = e0.elapsed_time(e1) / 10 / 1e3
+        iters = max(10, int(seconds / per))
+        for _ in range(iters // 3):
+            mm()
+        e0.record()
+        for _ in range(iters - iters // 3):
+            mm()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / 1e3
+        return 2.0 * n ** 3 * (iters - iters // 3) / t / 1e12
+    except (RuntimeError, AttributeError):
+        return None
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -316,6 +358,13 @@ def run_ours(args):
     else:
         peak, peak_src = (2 * 1400.0, "2x fallback bf16 sustained") if args.precision == "fp8" \
             else (1400.0, "fallback bf16 sustained")
+    peak_2x_bf16 = peak
+    fp8_peak = None
+    if args.precision == "fp8" and not args.no_fp8_peak:
+        fp8_peak = measure_fp8_peak(dev)
+        if fp8_peak:
+            peak, peak_src = fp8_peak, ("measured here: cuBLASLt e4m3 8192^3 (torch._scaled_mm), sustained "
+                                        "over ~1 s at the power cap")
     g = prof["gemm"]
     achieved = g["flops"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else 0.0
     traffic = GEMM_DRAM_BYTES_PER_EVAL.get((args.net, args.precision))
@@ -334,7 +383,8 @@ def run_ours(args):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic, "traffic_unit": "bytes per pass (DRAM, all GEMM launches)",
                          "kernel": "gemm_tc_kernel (all GEMM launches of one pass)",
-                         "peak_source": peak_src, "flops_per_eval": flops_per_eval(arch)},
+                         "peak_source": peak_src, "flops_per_eval": flops_per_eval(arch),
+                         "frac_of_2x_bf16": achieved / peak_2x_bf16 if args.precision == "fp8" else None},
             "kernel_ms": {k: round(v["ms"], 4) for k, v in prof.items()},
             "kernel_share": {k: round(v["ms"] / total_prof_ms, 4) for k, v in prof.items()} if total_prof_ms else {},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(B * (66 + 224 * 4)),
