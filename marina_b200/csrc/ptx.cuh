@@ -69,6 +69,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe: has the phase with parity `parity` of `bar` completed? (try_wait may park
+// the thread for a while; a role that polls several barriers uses this.)
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with parity `parity` of `bar` has completed. Gives up (returns
 // false) when `abort` is raised by another role of the CTA or after kWaitLimitNs; the
 // caller then raises `abort` itself and unwinds.
@@ -193,6 +207,18 @@ __device__ __forceinline__ void mma_bf16(uint32_t d, uint64_t a, uint64_t b, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T, bf16 x bf16 -> f32: A (M rows, one per TMEM lane, two bf16
+// of K per 32-bit column) is read from tensor memory.
+__device__ __forceinline__ void mma_bf16_tmem_a(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, e4m3 x e4m3 -> f32.
 __device__ __forceinline__ void mma_e4m3(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -225,6 +251,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+
+// Store 8 consecutive 32-bit TMEM columns of this thread's lane (32x32b shape, the warp's lane
+// quarter), a .sync.aligned warp instruction like the loads. Completion: tmem_wait_st.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  __syncwarp();
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
+      "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // The same for 16 consecutive columns.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
@@ -434,6 +471,8 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
 }
+// kind::f16 bf16 with B given N-major (MN-major: N contiguous in shared memory, K across rows).
+__host__ __device__ constexpr uint32_t idesc_bf16_bmn(int m, int n) { return idesc_bf16(m, n) | (1u << 16); }
 __host__ __device__ constexpr uint32_t idesc_e4m3(int m, int n) {
   return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
