@@ -524,7 +524,24 @@ int get_bucket(mrn_ctx* c, int n, Bucket** out) {
 }
 
 // Host-side input checks (the device kernels clamp as well, so bad input cannot fault).
+// Branch-free scan of every token and legal slot (vectorised by the compiler); the slow loop below
+// only runs to name the first offending entry.
+bool inputs_in_range(int n, const uint8_t* boards, const int32_t* legal) {
+  unsigned bad = 0;
+  for (int p = 0; p < n; ++p) {
+    const uint8_t* b = boards + static_cast<size_t>(p) * MRN_BOARD_BYTES;
+    for (int s = 0; s < 64; ++s) bad |= b[s] > 12;
+    bad |= (b[64] > 15) | (b[65] > 8);
+  }
+  if (legal) {
+    const size_t slots = static_cast<size_t>(n) * MRN_MAX_LEGAL;
+    for (size_t k = 0; k < slots; ++k) bad |= static_cast<uint32_t>(legal[k] + 1) > static_cast<uint32_t>(MRN_ACTIONS);
+  }
+  return bad == 0;
+}
+
 int validate_inputs(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal) {
+  if (inputs_in_range(n, boards, legal)) return MRN_OK;
   for (int p = 0; p < n; ++p) {
     const uint8_t* b = boards + static_cast<size_t>(p) * MRN_BOARD_BYTES;
     for (int s = 0; s < 64; ++s)
@@ -667,11 +684,10 @@ MRN_API int mrn_evaluate(mrn_ctx* c, int n, const uint8_t* boards, const int32_t
   if (n > c->max_batch) return c->fail(MRN_ERR_BATCH_TOO_LARGE, "batch of %d positions exceeds max_batch %d", n, c->max_batch);
   if (n == 0) return MRN_OK;
   if (!boards || !legal || !priors || !wdl) return c->fail(MRN_ERR_ARGUMENT, "NULL buffer");
-  int rc = validate_inputs(c, n, boards, legal);
-  if (rc) return rc;
   CK(cudaSetDevice(c->device));
   Bucket* b = nullptr;
-  if ((rc = get_bucket(c, n, &b))) return rc;
+  int rc = get_bucket(c, n, &b);
+  if (rc) return rc;
   const int P = b->positions;
   const bool direct_in = is_pinned(boards) && is_pinned(legal);
   const bool direct_out = is_pinned(priors) && is_pinned(wdl);
@@ -695,13 +711,18 @@ MRN_API int mrn_evaluate(mrn_ctx* c, int n, const uint8_t* boards, const int32_t
   CK(cudaMemcpyAsync(dst_p, c->priors, static_cast<size_t>(n) * MRN_MAX_LEGAL * 4, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(dst_w, c->wdl, static_cast<size_t>(n) * 3 * 4, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(c->h_status, c->status, 4, cudaMemcpyDeviceToHost, s));
+  // The inputs are checked while the GPU runs: the kernels clamp out-of-range tokens and flag
+  // out-of-range actions themselves, so a bad batch costs one wasted pass, never a fault; its
+  // outputs are discarded and the error names the first bad entry.
+  const int invalid = validate_inputs(c, n, boards, legal);
   CK(cudaStreamSynchronize(s));
   const int word = *c->h_status;
   if (word) {
     CK(cudaMemsetAsync(c->status, 0, 4, s));
     CK(cudaStreamSynchronize(s));
-    return check_status(c, word);
   }
+  if (invalid) return invalid;
+  if (word) return check_status(c, word);
   if (!direct_out) {
     memcpy(priors, c->h_priors, static_cast<size_t>(n) * MRN_MAX_LEGAL * 4);
     memcpy(wdl, c->h_wdl, static_cast<size_t>(n) * 3 * 4);
