@@ -28,8 +28,8 @@ CUDA_LIB = PKG / "libmarina_b200.so"
 CHESS_LIB = PKG / "libmarina_chess.so"
 
 CUDA_SOURCES = ["gemm.cu", "kernels.cu", "attention.cu", "runtime.cu", "static_forward.cu", "api_test.cu"]
-CUDA_HEADERS = ["ptx.cuh", "rows.cuh", "gemm.cuh", "gemm.h", "gemm_ln.cuh", "gemm_norm.cuh", "tmap.h", "kernels.cuh",
-                "runtime.h"]
+CUDA_HEADERS = ["ptx.cuh", "rows.cuh", "gemm.cuh", "gemm.h", "gemm_ln.cuh", "gemm_norm.cuh", "gemm_mlp.cuh", "tmap.h",
+                "kernels.cuh", "launch.h", "runtime.h"]
 CHESS_SOURCES = ["chess.cpp", "puct.cpp"]
 
 NVCC_FLAGS = [

@@ -25,6 +25,7 @@
 #include <stdlib.h>
 
 #include "kernels.cuh"
+#include "launch.h"
 #include "ptx.cuh"
 #include "tmap.h"
 
@@ -109,6 +110,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tma_prefetch_map(&map_qkv);
   }
   __syncthreads();
+  grid_dep_wait();
+  grid_dep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -349,6 +352,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();
+  grid_dep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -565,10 +570,8 @@ template <int HD, int T>
 cudaError_t launch_attention_t(const AttentionParams& p, const CUtensorMap& map, int grid, int items, cudaStream_t s) {
   constexpr int smem = attention_smem<HD, T>();
   if (p.out_type == ActType::kE4m3)
-    attention_kernel<HD, T, true><<<grid, kAttnThreads, smem, s>>>(map, p, items);
-  else
-    attention_kernel<HD, T, false><<<grid, kAttnThreads, smem, s>>>(map, p, items);
-  return cudaGetLastError();
+    return launch_kernel(attention_kernel<HD, T, true>, dim3(grid), dim3(kAttnThreads), smem, s, map, p, items);
+  return launch_kernel(attention_kernel<HD, T, false>, dim3(grid), dim3(kAttnThreads), smem, s, map, p, items);
 }
 
 template <int HD, int T>
@@ -608,10 +611,10 @@ cudaError_t launch_attention(const AttentionParams& p, int positions, int head_d
   const int grid = items < sms ? items : sms;
   if (head_dim == 64 && attention_tc_enabled()) {
     if (p.out_type == ActType::kE4m3)
-      attention_tc_kernel<true><<<grid, kTcThreads, attention_tc_smem(), s>>>(map, p, items);
-    else
-      attention_tc_kernel<false><<<grid, kTcThreads, attention_tc_smem(), s>>>(map, p, items);
-    return cudaGetLastError();
+      return launch_kernel(attention_tc_kernel<true>, dim3(grid), dim3(kTcThreads), attention_tc_smem(), s, map, p,
+                           items);
+    return launch_kernel(attention_tc_kernel<false>, dim3(grid), dim3(kTcThreads), attention_tc_smem(), s, map, p,
+                         items);
   }
   if (head_dim == 64) return launch_attention_t<64, 65>(p, map, grid, items, s);
   return launch_attention_t<32, 65>(p, map, grid, items, s);

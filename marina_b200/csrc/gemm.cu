@@ -7,6 +7,7 @@
 #include "gemm_ln.cuh"
 #include "gemm_mlp.cuh"
 #include "gemm_norm.cuh"
+#include "launch.h"
 #include "tmap.h"
 
 namespace mrn {
@@ -18,18 +19,16 @@ using ShapeOf = GemmShape<BN, Epi::kWarps, Epi::kOutBytes>;
 
 template <int BN, bool FP8, class Epi>
 cudaError_t launch_one(const GemmPlan& p, const Epi& epi, cudaStream_t stream) {
-  gemm_tc_kernel<BN, FP8, Epi><<<p.grid, ShapeOf<BN, Epi>::kThreads, ShapeOf<BN, Epi>::kSmemBytes, stream>>>(
-      p.map_a, p.map_b, p.map_out, epi, p.args.m, p.args.n, p.args.k, p.args.status);
-  return cudaGetLastError();
+  return launch_kernel(gemm_tc_kernel<BN, FP8, Epi>, dim3(p.grid), dim3(ShapeOf<BN, Epi>::kThreads),
+                       ShapeOf<BN, Epi>::kSmemBytes, stream, p.map_a, p.map_b, p.map_out, epi, p.args.m, p.args.n,
+                       p.args.k, p.args.status);
 }
 
 template <bool FP8, class Epi>
 cudaError_t launch_pair(const GemmPlan& p, const Epi& epi, cudaStream_t stream) {
   using P = PairShape<Epi::kOutBytes, Epi::kWarps>;
-  gemm_pair_kernel<FP8, Epi><<<p.grid, P::kThreads, P::kSmemBytes, stream>>>(p.map_a, p.map_b, p.map_out, epi,
-                                                                            p.args.m, p.args.n, p.args.k,
-                                                                            p.args.status);
-  return cudaGetLastError();
+  return launch_kernel(gemm_pair_kernel<FP8, Epi>, dim3(p.grid), dim3(P::kThreads), P::kSmemBytes, stream, p.map_a,
+                       p.map_b, p.map_out, epi, p.args.m, p.args.n, p.args.k, p.args.status);
 }
 
 template <bool FP8>
@@ -129,6 +128,7 @@ cudaError_t prepare_bn() {
 }
 
 // ---- residual GEMM + LayerNorm (gemm_ln.cuh): one cluster of n / BN CTAs per row block
+// `attr` has room for two attributes: the cluster shape and, when on, programmatic launch.
 cudaLaunchConfig_t ln_config(dim3 grid, int threads, int smem, int cluster, cudaStream_t stream,
                              cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
@@ -141,7 +141,7 @@ cudaLaunchConfig_t ln_config(dim3 grid, int threads, int smem, int cluster, cuda
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 1 + pdl_attribute(attr + 1);
   return cfg;
 }
 
@@ -150,7 +150,7 @@ cudaError_t launch_ln_bn(const GemmPlan& p, cudaStream_t stream) {
   using S = LnShape<BN>;
   const GemmArgs& a = p.args;
   const LnParams lp{a.bias, a.gamma, a.beta, static_cast<const __half*>(a.out), a.scale, a.eps, a.ln_inv_q, a.n};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   const cudaLaunchConfig_t cfg = ln_config(dim3(p.grid, 1, 1), S::kThreads, S::kSmemBytes, p.cluster, stream, attr);
   return cudaLaunchKernelEx(&cfg, gemm_ln_kernel<BN, FP8, FP8>, p.map_a, p.map_b, p.map_out, p.map_aux, lp, a.m, a.k,
                             a.status);
@@ -170,7 +170,7 @@ cudaError_t launch_ln(const GemmPlan& p, cudaStream_t stream) {
 template <int BN, bool FP8>
 int ln_max_clusters(int cluster) {
   using S = LnShape<BN>;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   const cudaLaunchConfig_t cfg = ln_config(dim3(cluster, 1, 1), S::kThreads, S::kSmemBytes, cluster, nullptr, attr);
   int n = 0;
   if (cudaOccupancyMaxActiveClusters(&n, gemm_ln_kernel<BN, FP8, FP8>, &cfg) != cudaSuccess) {
@@ -204,9 +204,8 @@ cudaError_t launch_norm(const GemmPlan& p, const Epi& epi, cudaStream_t stream) 
   using S = NormShape<Epi::kOutBytes, Epi::kWarps>;
   const GemmArgs& a = p.args;
   const NormA na{static_cast<const __half*>(a.norm_x), a.gamma, a.beta, a.eps, a.ln_inv_q};
-  gemm_norm_kernel<Epi><<<p.grid, S::kThreads, S::kSmemBytes, stream>>>(p.map_b, p.map_out, epi, na, a.m, a.n,
-                                                                        a.status);
-  return cudaGetLastError();
+  return launch_kernel(gemm_norm_kernel<Epi>, dim3(p.grid), dim3(S::kThreads), S::kSmemBytes, stream, p.map_b,
+                       p.map_out, epi, na, a.m, a.n, a.status);
 }
 
 cudaError_t launch_norm_epi(const GemmPlan& p, cudaStream_t stream) {
@@ -252,9 +251,9 @@ bool plan_norm(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
 template <class Gelu>
 cudaError_t launch_mlp(const MlpPlan& p, const Gelu& gelu, cudaStream_t stream) {
   const MlpArgs& a = p.args;
-  gemm_mlp_kernel<Gelu><<<p.grid, MlpShape::kThreads, MlpShape::kSmemBytes, stream>>>(
-      p.map_h, p.map_w1, p.map_w2, static_cast<__half*>(a.x), gelu, EpiResidual{a.b2, a.s2}, a.m, a.ff, a.status);
-  return cudaGetLastError();
+  return launch_kernel(gemm_mlp_kernel<Gelu>, dim3(p.grid), dim3(MlpShape::kThreads), MlpShape::kSmemBytes, stream,
+                       p.map_h, p.map_w1, p.map_w2, static_cast<__half*>(a.x), gelu, EpiResidual{a.b2, a.s2}, a.m,
+                       a.ff, a.status);
 }
 
 template <class Gelu>

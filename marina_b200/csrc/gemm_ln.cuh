@@ -168,6 +168,8 @@ __global__ void __launch_bounds__(LnShape<BN>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();
+  grid_dep_launch();
 
   if (warp == 0) {
     if (lane == 0) {

@@ -156,6 +156,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(MlpShape::kThreads, 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();
+  grid_dep_launch();
 
   if (warp == 0) {
     if (lane == 0) {

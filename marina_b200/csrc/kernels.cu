@@ -8,6 +8,7 @@
 #include <type_traits>
 
 #include "kernels.cuh"
+#include "launch.h"
 #include "ptx.cuh"
 #include "rows.cuh"
 
@@ -29,6 +30,8 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedParams e, NormParams
     gb[d + k] = n.beta[k] * oq;
   }
   __syncthreads();
+  grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -93,6 +96,8 @@ __global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel
     gb[d + i] = n.beta[i] * oq;
   }
   __syncthreads();
+  grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   const int stride = gridDim.x * 8;
   int row = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -133,6 +138,8 @@ __global__ void __launch_bounds__(kHeadsWarps * 32) heads_kernel(HeadsParams p, 
   const int pos = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t row0 = static_cast<size_t>(pos) * p.t;
+  grid_dep_wait();
+  grid_dep_launch();
 
   if (warp == 0) {
     Row r;
@@ -200,6 +207,8 @@ __global__ void __launch_bounds__(kHeadsWarps * 32) heads_kernel(HeadsParams p, 
 // Value head output layer and softmax, one warp per position (src/net/cpu.rs:161-162,179-180).
 template <int VPL, int VEC>
 __global__ void __launch_bounds__(256) value_out_kernel(ValueOutParams p, int positions, int d) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   const int pos = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (pos >= positions) return;
@@ -254,8 +263,8 @@ template <int VPL, int VEC>
 struct EmbedLaunch {
   static cudaError_t run(int d, const EmbedParams& e, const NormParams& n, int positions, cudaStream_t s) {
     const int rows = positions * e.t;
-    embed_ln_kernel<VPL, VEC><<<(rows + 7) / 8, 256, 2 * d * sizeof(float), s>>>(e, n, rows, d);
-    return cudaGetLastError();
+    return launch_kernel(embed_ln_kernel<VPL, VEC>, dim3((rows + 7) / 8), dim3(256), 2 * d * sizeof(float), s, e, n,
+                         rows, d);
   }
 };
 
@@ -268,8 +277,7 @@ struct NormLaunch {
     const int blocks_needed = (rows + 7) / 8;
     const int resident = sms * ln_blocks_per_sm<VPL>();
     const int grid = blocks_needed < resident ? blocks_needed : resident;
-    layernorm_kernel<VPL, VEC><<<grid, 256, 2 * d * sizeof(float), s>>>(x, n, rows, d);
-    return cudaGetLastError();
+    return launch_kernel(layernorm_kernel<VPL, VEC>, dim3(grid), dim3(256), 2 * d * sizeof(float), s, x, n, rows, d);
   }
 };
 
@@ -277,16 +285,14 @@ template <int VPL, int VEC>
 struct HeadsLaunch {
   static cudaError_t run(int d, const HeadsParams& p, int positions, cudaStream_t s) {
     const size_t smem = p.softmax ? sizeof(float) * p.slots : 0;
-    heads_kernel<VPL, VEC><<<positions, kHeadsWarps * 32, smem, s>>>(p, d);
-    return cudaGetLastError();
+    return launch_kernel(heads_kernel<VPL, VEC>, dim3(positions), dim3(kHeadsWarps * 32), smem, s, p, d);
   }
 };
 
 template <int VPL, int VEC>
 struct ValueOutLaunch {
   static cudaError_t run(int d, const ValueOutParams& p, int positions, cudaStream_t s) {
-    value_out_kernel<VPL, VEC><<<(positions + 7) / 8, 256, 0, s>>>(p, positions, d);
-    return cudaGetLastError();
+    return launch_kernel(value_out_kernel<VPL, VEC>, dim3((positions + 7) / 8), dim3(256), 0, s, p, positions, d);
   }
 };
 

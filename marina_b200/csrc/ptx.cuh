@@ -38,6 +38,19 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   return t;
 }
 
+// ---- programmatic dependent launch ---------------------------------------------------------
+// A kernel launched with programmatic stream serialisation may start while the kernel before
+// it on the stream is still running. It sets up what needs nothing an earlier kernel writes
+// (shared memory, barriers, TMEM, descriptor prefetch, the constant weights), then waits here
+// until the grids it depends on have completed and their writes are visible; every other
+// global read, and every global write, comes after. Without a programmatic dependency the wait
+// returns at once.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Lets the next kernel on the stream begin launching once every block of this grid has
+// signalled (or exited); its blocks still wait for this grid's completion in grid_dep_wait.
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- mbarrier ---------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

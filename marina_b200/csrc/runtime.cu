@@ -17,6 +17,7 @@
 #include "../../include/marina_b200.h"
 #include "gemm.h"
 #include "kernels.cuh"
+#include "launch.h"
 #include "runtime.h"
 
 namespace {
@@ -248,6 +249,22 @@ bool ln_fusion_enabled() {
   return on;
 }
 
+// Programmatic dependent launch between the kernels of a pass. MRN_PDL=1: always; MRN_PDL=0:
+// never; unset: for batches of up to kPdlMaxPositions positions. Measured on B200 (small net,
+// e4m3): it takes 13% off the latency of a 1-position pass (0.490 -> 0.425 ms), 8-10% at 16-64
+// positions and 2% at 256, where each kernel lasts microseconds and the gaps between them
+// count; from 1024 positions on the pass runs at the power cap and came out 1-3% slower with
+// the gaps closed, so it stays off there.
+constexpr int kPdlMaxPositions = 256;
+
+bool pdl_enabled(int positions) {
+  static const int mode = [] {
+    const char* e = getenv("MRN_PDL");
+    return e && e[0] == '0' ? 0 : e && e[0] == '1' ? 1 : -1;
+  }();
+  return mode == 1 || (mode == -1 && positions <= kPdlMaxPositions);
+}
+
 bool mlp_enabled() {
   static const bool on = [] {
     const char* e = getenv("MRN_MLP");
@@ -435,6 +452,10 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
   CK(mrn::launch_embed_ln(
       e, mrn::NormParams{D0.n1g, D0.n1b, c->eps, b.embed_norm ? c->h : nullptr, act, 1.f / D0.as[0]}, P, d, s));
   done();
+  // Every later kernel follows a kernel of this pass, so its launch may overlap the end of that
+  // one (the embedding follows the input copies and launches plainly). Not while profiling:
+  // the per-launch events would time overlapping kernels.
+  const mrn::PdlScope pdl(!prof && mrn::pdl_enabled(P));
   const mrn::LayerBuffers bufs{c->h, c->qkv, c->attn, c->ff, c->x};
   for (int l = 0; l < c->layers; ++l) {
     const DevLayer& D = c->dl[l];

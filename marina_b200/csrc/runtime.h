@@ -143,6 +143,10 @@ void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, b
 bool mlp_args(const GemmArgs& ffn1, const GemmArgs& ffn2, MlpArgs* out);
 // Whether FFN1 + FFN2 run as one fused launch (environment MRN_MLP=1; off by default).
 bool mlp_enabled();
+// Whether the kernels after the first of a pass over `positions` positions launch with
+// programmatic dependent launch (environment MRN_PDL: 1 always, 0 never; by default for small
+// batches).
+bool pdl_enabled(int positions);
 // Whether layer l's QKV GEMM computes norm1 itself (under the same `norm` setting).
 bool qkv_normalises(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool norm);
 // Whether plans use the fused residual + LayerNorm epilogue (environment MRN_GEMM_LN=1; off by default).

@@ -32,6 +32,7 @@
 #include "../../include/marina_b200.h"
 #include "gemm.h"
 #include "kernels.cuh"
+#include "launch.h"
 #include "runtime.h"
 
 namespace {
@@ -153,6 +154,8 @@ int forward(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, floa
       mrn::NormParams{D0.n1g, D0.n1b, c->eps, mrn::qkv_normalises(c, 0, R, bufs, norm) ? nullptr : h, act,
                       1.f / D0.as[0]},
       n, d, s));
+  // The kernels after the embedding follow one of this pass: their launches may overlap.
+  const mrn::PdlScope pdl(mrn::pdl_enabled(n));
   for (int l = 0; l < c->layers; ++l) {
     const mrn::DevLayer& D = c->dl[l];
     mrn::GemmArgs g[4];

@@ -380,3 +380,20 @@ def test_fused_mlp_plans(tmp_path, net, precision):
     else:
         assert m["wdl"] == 0 and m["prior"] == 0, m
     _check_plans_against_oracle(outs, net, precision)
+
+
+@pytest.mark.parametrize("net,precision,extra", [
+    ("small", "fp8", {}),
+    ("nano", "bf16", {}),
+    ("small", "fp8", {"MRN_GEMM_NORM": "1", "MRN_MLP": "1", "MRN_ATTN_TC": "1"}),
+    ("small", "bf16", {"MRN_GEMM_LN": "1"}),
+])
+def test_programmatic_launch_changes_no_result(tmp_path, net, precision, extra):
+    """Kernels launched with programmatic dependent launch (MRN_PDL=1: each kernel's launch and
+    set-up overlap the end of the previous one, and it waits for that grid before touching memory)
+    give the same bits as plain stream-ordered launches (MRN_PDL=0), for the default plans and for
+    the opt-in kernels."""
+    outs = _run_plans(tmp_path, net, precision, {"plain": dict(extra, MRN_PDL="0"), "pdl": dict(extra, MRN_PDL="1")})
+    assert int(outs["plain"]["launches"]) == int(outs["pdl"]["launches"])
+    assert np.array_equal(outs["plain"]["priors"], outs["pdl"]["priors"])
+    assert np.array_equal(outs["plain"]["wdl"], outs["pdl"]["wdl"])
