@@ -119,8 +119,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       uint32_t issued = 0, parities = 0;  // per buffer: a load is in flight / its phase parity
       for (int k = 0; static_cast<int>(blockIdx.x) + k * G < items && !*abort; ++k) {
         const int item = static_cast<int>(blockIdx.x) + k * G;
-        const int team = k % kTeams, j = k / kTeams, buf = j & 1, slot = team * kBufs + buf;
-        const uint32_t par = (j >> 1) & 1;
+        const int team = k % kTeams, j = k / kTeams, buf = j % kBufs, slot = team * kBufs + buf;
+        const uint32_t par = (j / kBufs) & 1;
         if (!mbar_wait(&empty[slot], par ^ 1u, abort)) {
           raise_error(p.status, abort, kErrTimeoutAttention);
           break;
@@ -149,8 +149,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const float scale_log2 = rsqrtf(static_cast<float>(HD)) * 1.4426950408889634f;
     for (int k = team; static_cast<int>(blockIdx.x) + k * G < items; k += kTeams) {
       const int item = static_cast<int>(blockIdx.x) + k * G;
-      const int j = k / kTeams, buf = j & 1, slot = team * kBufs + buf;
-      if (!mbar_wait(&full[slot], (j >> 1) & 1, abort)) {
+      const int j = k / kTeams, buf = j % kBufs, slot = team * kBufs + buf;
+      if (!mbar_wait(&full[slot], (j / kBufs) & 1, abort)) {
         if (lane == 0) raise_error(p.status, abort, kErrTimeoutAttention);
         break;
       }
