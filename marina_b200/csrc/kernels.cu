@@ -123,15 +123,23 @@ __global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel
 }
 
 // ---- heads -----------------------------------------------------------------------------
-// One CTA (8 warps) per position. Each warp takes legal slots in turn: the slot's square token
+// One CTA (8 warps) per position. Each warp takes every 8th legal slot: the slot's square token
 // gets the final norm and the policy norm in registers (src/net/cpu.rs:137,140-152) and its
 // logit is bias[plane] + <token, W[plane]> (src/net/cuda/kernels.cu:407-444 gathers the same
 // logits). Warp 0 also normalises the state token for the value head's first layer. The
 // softmax over the legal slots is block-wide (src/net/cpu.rs:177-178).
 constexpr int kHeadsWarps = 8;
 
+// Two slots in flight take 2 x 2 rows of VPL values per thread. Blocks per SM for the register
+// bound: the most at which the rows stay in registers (d = 192 and 512: three blocks, 80
+// registers), one block from d = 768.
+template <int VPL>
+constexpr int heads_blocks_per_sm() {
+  return VPL >= 24 ? 1 : (VPL <= 8 || VPL == 16) ? 3 : 2;
+}
+
 template <int VPL, int VEC>
-__global__ void __launch_bounds__(kHeadsWarps * 32) heads_kernel(HeadsParams p, int d) {
+__global__ void __launch_bounds__(kHeadsWarps * 32, heads_blocks_per_sm<VPL>()) heads_kernel(HeadsParams p, int d) {
   extern __shared__ float logits[];  // [slots] when p.softmax
   __shared__ float red[kHeadsWarps];
   using Row = WarpRow<VPL, VEC>;
@@ -149,30 +157,51 @@ __global__ void __launch_bounds__(kHeadsWarps * 32) heads_kernel(HeadsParams p, 
     r.store_act(static_cast<__nv_bfloat16*>(p.value_in) + static_cast<size_t>(pos) * d, ActType::kBf16, 1.f, lane);
   }
 
-  for (int slot = warp; slot < p.slots; slot += kHeadsWarps) {
-    const int action = p.legal ? p.legal[static_cast<size_t>(pos) * p.slots + slot] : slot;
-    float logit = -INFINITY;
-    if (action >= kActions) {
-      if (lane == 0 && p.status) atomicCAS(p.status, 0, kErrBadAction);
-    } else if (action >= 0) {
-      const int square = action / kPlanes, plane = action - square * kPlanes;
-      Row r;
-      r.load(p.x + (row0 + p.square_start + square) * d, lane);
-      ln_apply(r, p.final_g, p.final_b, ln_stats(r, d, p.eps), lane);
-      ln_apply(r, p.policy_g, p.policy_b, ln_stats(r, d, p.eps), lane);
-      Row w;  // the plane's weight row, vector loads
-      w.load(p.policy_w + static_cast<size_t>(plane) * d, lane);
-      float2 acc = make_float2(0.f, 0.f);
+  // Warp w owns slots w, w + 8, ...: one coalesced read gives it the actions of 32 of them
+  // (lane i holds slot base + 8 i), padding and out-of-range slots get -inf at once, and the
+  // legal ones are evaluated two at a time, so each warp's chain of dependent loads and
+  // reductions is half as long as one slot after another.
+  auto put = [&](int slot, float logit) {
+    if (p.softmax)
+      logits[slot] = logit;
+    else
+      p.priors[static_cast<size_t>(pos) * p.slots + slot] = logit;
+  };
+  auto logit_of = [&](int plane, Row& r, const Row& w) {
+    ln_apply(r, p.final_g, p.final_b, ln_stats(r, d, p.eps), lane);
+    ln_apply(r, p.policy_g, p.policy_b, ln_stats(r, d, p.eps), lane);
+    float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int k = 0; k < VPL; k += 2)
-        acc = fma2(make_float2(r.v[k], r.v[k + 1]), make_float2(w.v[k], w.v[k + 1]), acc);
-      logit = warp_sum(acc.x + acc.y) + __ldg(p.policy_bias + plane);
+    for (int k = 0; k < VPL; k += 2)
+      acc = fma2(make_float2(r.v[k], r.v[k + 1]), make_float2(w.v[k], w.v[k + 1]), acc);
+    return warp_sum(acc.x + acc.y) + __ldg(p.policy_bias + plane);
+  };
+  for (int base = warp; base < p.slots; base += 32 * kHeadsWarps) {
+    const int slot = base + kHeadsWarps * lane;
+    int action = -1;
+    if (slot < p.slots) action = p.legal ? p.legal[static_cast<size_t>(pos) * p.slots + slot] : slot;
+    if (action >= kActions) {
+      if (p.status) atomicCAS(p.status, 0, kErrBadAction);
+      action = -1;
     }
-    if (lane == 0) {
-      if (p.softmax)
-        logits[slot] = logit;
-      else
-        p.priors[static_cast<size_t>(pos) * p.slots + slot] = logit;
+    if (slot < p.slots && action < 0) put(slot, -INFINITY);
+    unsigned todo = __ballot_sync(~0u, action >= 0);
+    while (todo) {
+      const int l1 = __ffs(todo) - 1;
+      todo &= todo - 1;
+      const int l2 = todo ? __ffs(todo) - 1 : l1;  // an odd last slot is computed twice
+      todo &= todo - 1;
+      const int a1 = __shfl_sync(~0u, action, l1), a2 = __shfl_sync(~0u, action, l2);
+      Row r1, r2, w1, w2;
+      r1.load(p.x + (row0 + p.square_start + a1 / kPlanes) * d, lane);
+      r2.load(p.x + (row0 + p.square_start + a2 / kPlanes) * d, lane);
+      w1.load(p.policy_w + static_cast<size_t>(a1 % kPlanes) * d, lane);
+      w2.load(p.policy_w + static_cast<size_t>(a2 % kPlanes) * d, lane);
+      const float z1 = logit_of(a1 % kPlanes, r1, w1), z2 = logit_of(a2 % kPlanes, r2, w2);
+      if (lane == 0) {
+        put(base + kHeadsWarps * l1, z1);
+        if (l2 != l1) put(base + kHeadsWarps * l2, z2);
+      }
     }
   }
   if (!p.softmax) return;
