@@ -144,6 +144,15 @@ MRN_API int mrn_create(const mrn_arch* arch, const mrn_weights* weights, int dev
  * is priors[p*224 .. p*224 + legal_count] and wdl[p*3 .. p*3+3] (:994-999). */
 MRN_API int mrn_evaluate(mrn_ctx* ctx, int n, const uint8_t* boards, const int32_t* legal, float* priors, float* wdl);
 
+/* `mrn_evaluate` with the priors returned as IEEE half-precision bit patterns (n x MRN_MAX_LEGAL
+ * uint16_t, rounded to nearest on the device), halving the bytes copied back per position from
+ * 896 to 448; `wdl` stays f32. The output format the reference's `Evaluation` gets is f32
+ * (src/net/mod.rs:266-271), so a caller widens the legal slots it reads; the half rounding
+ * (relative 2^-11) is far inside the priors' tolerance. The first call allocates a
+ * max_batch x 224 x 2-byte device buffer. */
+MRN_API int mrn_evaluate_f16(mrn_ctx* ctx, int n, const uint8_t* boards, const int32_t* legal, uint16_t* priors,
+                             float* wdl);
+
 /* Raw logits over all MRN_ACTIONS actions (`policy`, n x 4672, action-index order) and the
  * WDL logits (`value`, n x 3), the analogue of `CpuNetwork::logits` (src/net/cpu.rs:40-46)
  * for parity checks. */

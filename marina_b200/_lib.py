@@ -28,7 +28,7 @@ PROFILE_SLOTS = ("embed", "layernorm", "gemm", "attention", "heads")
 
 # Every symbol the header declares; `tests/test_abi.py` checks the library exports them.
 EXPORTS = (
-    "mrn_create", "mrn_evaluate", "mrn_logits", "mrn_evaluate_device", "mrn_status_word",
+    "mrn_create", "mrn_evaluate", "mrn_evaluate_f16", "mrn_logits", "mrn_evaluate_device", "mrn_status_word",
     "mrn_profile", "mrn_launches_per_forward", "mrn_describe", "mrn_last_error", "mrn_destroy",
     "mrn_test_gemm", "mrn_test_gemm_ln", "mrn_test_gemm_norm", "mrn_test_mlp", "mrn_test_attention", "mrn_test_layernorm",
     "mrn_test_last_error",
@@ -77,6 +77,7 @@ def load() -> ctypes.CDLL:
     sig = {
         "mrn_create": (c_int, [POINTER(MrnArch), POINTER(MrnWeights), c_int, c_int, c_int, POINTER(c_void_p)]),
         "mrn_evaluate": (c_int, [c_void_p, c_int, POINTER(c_uint8), POINTER(c_int32), POINTER(c_float), POINTER(c_float)]),
+        "mrn_evaluate_f16": (c_int, [c_void_p, c_int, POINTER(c_uint8), POINTER(c_int32), c_void_p, POINTER(c_float)]),
         "mrn_logits": (c_int, [c_void_p, c_int, POINTER(c_uint8), POINTER(c_float), POINTER(c_float)]),
         "mrn_evaluate_device": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
         "mrn_evaluate_device_static": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),

@@ -325,6 +325,18 @@ struct ValueOutLaunch {
   }
 };
 
+// Four priors per thread: one 16-byte read, one 8-byte write.
+__global__ void __launch_bounds__(256) priors_to_half_kernel(const float* __restrict__ in, __half* __restrict__ out,
+                                                             int quads) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int i = blockIdx.x * 256 + threadIdx.x;
+  if (i >= quads) return;
+  const float4 v = reinterpret_cast<const float4*>(in)[i];
+  __half2 h[2] = {__floats2half2_rn(v.x, v.y), __floats2half2_rn(v.z, v.w)};
+  reinterpret_cast<uint2*>(out)[i] = *reinterpret_cast<const uint2*>(h);
+}
+
 }  // namespace
 
 cudaError_t launch_embed_ln(const EmbedParams& e, const NormParams& n, int positions, int d, cudaStream_t s) {
@@ -341,6 +353,12 @@ cudaError_t launch_heads(const HeadsParams& p, int positions, int d, cudaStream_
 
 cudaError_t launch_value_out(const ValueOutParams& p, int positions, int d, cudaStream_t s) {
   return dispatch_d<ValueOutLaunch>(d, p, positions, s);
+}
+
+cudaError_t launch_priors_to_half(const float* in, __half* out, int count, cudaStream_t s) {
+  if (count <= 0 || count % 4 != 0) return cudaErrorInvalidValue;
+  const int quads = count / 4;
+  return launch_kernel(priors_to_half_kernel, dim3((quads + 255) / 256), dim3(256), 0, s, in, out, quads);
 }
 
 }  // namespace mrn

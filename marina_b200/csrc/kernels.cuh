@@ -82,6 +82,10 @@ struct ValueOutParams {
 };
 cudaError_t launch_value_out(const ValueOutParams& p, int positions, int d, cudaStream_t s);
 
+// out[i] = f16(in[i]) (round to nearest) for count values, count a multiple of 4, both buffers
+// 16-byte aligned: the priors in half precision for the host copy.
+cudaError_t launch_priors_to_half(const float* in, __half* out, int count, cudaStream_t s);
+
 // Device error codes raised by these kernels (the GEMM uses 1..4).
 constexpr int kErrBadAction = 16;
 

@@ -695,11 +695,12 @@ MRN_API int mrn_create(const mrn_arch* arch, const mrn_weights* weights, int dev
   return MRN_OK;
 }
 
-MRN_API int mrn_evaluate(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, float* priors, float* wdl) {
-  if (!c) {
-    g_create_error = "context is NULL";
-    return MRN_ERR_ARGUMENT;
-  }
+namespace {
+
+// The pass on host buffers behind mrn_evaluate (f32 priors) and mrn_evaluate_f16 (`half`: the
+// priors converted to f16 on the device, so the copy back moves half the bytes).
+int evaluate_host(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, void* priors, bool half,
+                  float* wdl) {
   std::lock_guard<std::mutex> lock(c->mu);
   if (n < 0) return c->fail(MRN_ERR_ARGUMENT, "n = %d", n);
   if (n > c->max_batch) return c->fail(MRN_ERR_BATCH_TOO_LARGE, "batch of %d positions exceeds max_batch %d", n, c->max_batch);
@@ -709,7 +710,11 @@ MRN_API int mrn_evaluate(mrn_ctx* c, int n, const uint8_t* boards, const int32_t
   Bucket* b = nullptr;
   int rc = get_bucket(c, n, &b);
   if (rc) return rc;
+  if (half && !c->priors16 &&
+      (rc = dev_alloc(c, &c->priors16, static_cast<size_t>(c->max_bucket) * MRN_MAX_LEGAL * 2)))
+    return rc;
   const int P = b->positions;
+  const size_t prior_bytes = static_cast<size_t>(n) * MRN_MAX_LEGAL * (half ? 2 : 4);
   const bool direct_in = is_pinned(boards) && is_pinned(legal);
   const bool direct_out = is_pinned(priors) && is_pinned(wdl);
   const uint8_t* src_b = boards;
@@ -727,9 +732,11 @@ MRN_API int mrn_evaluate(mrn_ctx* c, int n, const uint8_t* boards, const int32_t
     CK(cudaMemsetAsync(c->legal + static_cast<size_t>(n) * MRN_MAX_LEGAL, 0xff, static_cast<size_t>(P - n) * MRN_MAX_LEGAL * 4, s));
   }
   CK(cudaGraphLaunch(b->graph, s));
-  float* dst_p = direct_out ? priors : c->h_priors;
+  if (half) CK(mrn::launch_priors_to_half(c->priors, c->priors16, n * MRN_MAX_LEGAL, s));
+  void* dst_p = direct_out ? priors : static_cast<void*>(c->h_priors);
   float* dst_w = direct_out ? wdl : c->h_wdl;
-  CK(cudaMemcpyAsync(dst_p, c->priors, static_cast<size_t>(n) * MRN_MAX_LEGAL * 4, cudaMemcpyDeviceToHost, s));
+  const void* src_p = half ? static_cast<const void*>(c->priors16) : static_cast<const void*>(c->priors);
+  CK(cudaMemcpyAsync(dst_p, src_p, prior_bytes, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(dst_w, c->wdl, static_cast<size_t>(n) * 3 * 4, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(c->h_status, c->status, 4, cudaMemcpyDeviceToHost, s));
   // The inputs are checked while the GPU runs: the kernels clamp out-of-range tokens and flag
@@ -745,10 +752,29 @@ MRN_API int mrn_evaluate(mrn_ctx* c, int n, const uint8_t* boards, const int32_t
   if (invalid) return invalid;
   if (word) return check_status(c, word);
   if (!direct_out) {
-    memcpy(priors, c->h_priors, static_cast<size_t>(n) * MRN_MAX_LEGAL * 4);
+    memcpy(priors, c->h_priors, prior_bytes);
     memcpy(wdl, c->h_wdl, static_cast<size_t>(n) * 3 * 4);
   }
   return MRN_OK;
+}
+
+}  // namespace
+
+MRN_API int mrn_evaluate(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, float* priors, float* wdl) {
+  if (!c) {
+    g_create_error = "context is NULL";
+    return MRN_ERR_ARGUMENT;
+  }
+  return evaluate_host(c, n, boards, legal, priors, false, wdl);
+}
+
+MRN_API int mrn_evaluate_f16(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, uint16_t* priors,
+                             float* wdl) {
+  if (!c) {
+    g_create_error = "context is NULL";
+    return MRN_ERR_ARGUMENT;
+  }
+  return evaluate_host(c, n, boards, legal, priors, true, wdl);
 }
 
 MRN_API int mrn_logits(mrn_ctx* c, int n, const uint8_t* boards, float* policy, float* value) {

@@ -107,6 +107,7 @@ struct mrn_ctx {
   float* wdl = nullptr;
   int* status = nullptr;
   float* logits = nullptr;  // [max_bucket, 4672], allocated by the first mrn_logits
+  __half* priors16 = nullptr;  // [max_bucket, 224], allocated by the first mrn_evaluate_f16
   // pinned staging
   uint8_t* h_boards = nullptr;
   int32_t* h_legal = nullptr;

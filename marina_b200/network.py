@@ -177,6 +177,21 @@ class B200Network(Network):
         self._check(rc, "forward")
         return priors, wdl
 
+    def evaluate_packed_f16(self, boards: np.ndarray, legal: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+        """`mrn_evaluate_f16`: as `evaluate_packed`, with the priors returned as float16 [n, 224]
+        (half the bytes copied back from the GPU)."""
+        boards = np.ascontiguousarray(boards, dtype=np.uint8)
+        legal = np.ascontiguousarray(legal, dtype=np.int32)
+        n = boards.shape[0]
+        if boards.shape != (n, BOARD_BYTES) or legal.shape != (n, MAX_LEGAL):
+            raise ValueError("boards must be [n, 66] and legal [n, 224]")
+        priors = np.empty((n, MAX_LEGAL), dtype=np.float16)
+        wdl = np.empty((n, 3), dtype=np.float32)
+        rc = self._lib.mrn_evaluate_f16(self._ctx, n, boards.ctypes.data_as(POINTER(c_uint8)),
+                                        legal.ctypes.data_as(POINTER(c_int32)), priors.ctypes.data, _f32p(wdl))
+        self._check(rc, "forward")
+        return priors, wdl
+
     def logits(self, boards: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
         """Raw policy logits [n, 4672] and WDL logits [n, 3] (`CpuNetwork::logits`)."""
         boards = np.ascontiguousarray(boards, dtype=np.uint8)

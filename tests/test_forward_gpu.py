@@ -107,6 +107,38 @@ def test_small_config_batch_256(small_setup, precision):
     check(compare(priors, wdl, ref_p, ref_w, counts), precision)
 
 
+def test_f16_priors_are_the_f32_priors_rounded(small_setup):
+    """mrn_evaluate_f16 returns exactly the f32 priors rounded to nearest-even half precision
+    (what numpy's float16 conversion does), the same WDL bits, zeros on padding, and meets the
+    oracle bounds once widened; through pageable and pinned host buffers, two calls in a row."""
+    import torch
+
+    arch, w, boards, legal, counts, ref, ref_q = small_setup
+    net = B200Network(arch, w, max_batch=256, precision="fp8")
+    p32, w32 = net.evaluate_packed(boards, legal)
+    for _ in range(2):
+        p16, w16 = net.evaluate_packed_f16(boards, legal)
+        assert p16.dtype == np.float16 and p16.shape == p32.shape
+        assert np.array_equal(p16, p32.astype(np.float16))
+        assert np.array_equal(w16, w32)
+    check(compare(p16.astype(np.float32), w16, ref_q[0], ref_q[1], counts) | {"sums": 0.0}, "fp8")
+    sums = [abs(float(p16[p, :c].astype(np.float64).sum()) - 1) for p, c in enumerate(counts)]
+    assert max(sums) < 224 * 2.0 ** -11, max(sums)
+    n = len(counts)
+    hp = torch.empty((n, 224), dtype=torch.float16, pin_memory=True)
+    hw = torch.empty((n, 3), dtype=torch.float32, pin_memory=True)
+    hb = torch.from_numpy(np.ascontiguousarray(boards)).pin_memory()
+    hl = torch.from_numpy(np.ascontiguousarray(legal)).pin_memory()
+    from ctypes import POINTER, c_float, c_int32, c_uint8, cast, c_void_p
+
+    rc = net._lib.mrn_evaluate_f16(net._ctx, n, cast(c_void_p(hb.data_ptr()), POINTER(c_uint8)),
+                                   cast(c_void_p(hl.data_ptr()), POINTER(c_int32)), hp.data_ptr(),
+                                   cast(c_void_p(hw.data_ptr()), POINTER(c_float)))
+    assert rc == 0
+    assert np.array_equal(hp.numpy(), p16) and np.array_equal(hw.numpy(), w32)
+    net.close()
+
+
 @pytest.mark.parametrize("net,precision", [("nano", "bf16"), ("nano", "fp8w"), ("small", "fp8w"), ("small", "fp8")])
 def test_argmax_agreement_on_1024_positions(net, precision):
     """The argmax criterion on a sample large enough for a 1% bound to mean something."""
