@@ -435,13 +435,18 @@ def run_sweep(args):
         for _ in range(args.steps):
             net.evaluate_packed(boards[:b], legal[:b])
         e2e_ms = (time.perf_counter() - t0) / args.steps * 1e3
+        net.evaluate_packed_f16(boards[:b], legal[:b])  # the first call allocates its device buffer
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            net.evaluate_packed_f16(boards[:b], legal[:b])
+        e2e_f16_ms = (time.perf_counter() - t0) / args.steps * 1e3
         prof = net.profile(b, d_boards.data_ptr(), d_legal.data_ptr(), d_priors.data_ptr(), d_wdl.data_ptr(),
                            stream.cuda_stream)
         g = prof["gemm"]
         p50 = float(np.median(times))
         print(json.dumps({"mode": "sweep", "net": args.net, "precision": args.precision, "batch": b,
                           "latency_ms_p50": p50, "evals_per_s": b / (p50 / 1e3), "e2e_latency_ms": e2e_ms,
-                          "e2e_evals_per_s": b / (e2e_ms / 1e3), "gemm_tflops": g["flops"] / (g["ms"] / 1e3) / 1e12,
+                          "e2e_evals_per_s": b / (e2e_ms / 1e3), "e2e_f16_latency_ms": e2e_f16_ms, "gemm_tflops": g["flops"] / (g["ms"] / 1e3) / 1e12,
                           "kernel_ms": {k: round(v["ms"], 4) for k, v in prof.items()}}), flush=True)
     net.close()
 
