@@ -131,8 +131,8 @@ __global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel
 constexpr int kHeadsWarps = 8;
 
 // Two slots in flight take 2 x 2 rows of VPL values per thread. Blocks per SM for the register
-// bound: the most at which the rows stay in registers (d = 192 and 512: three blocks, 80
-// registers), one block from d = 768.
+// bound: the most at which the rows stay in registers (three blocks for d = 192 and d = 512,
+// which then takes 80 registers; one block from d = 768).
 template <int VPL>
 constexpr int heads_blocks_per_sm() {
   return VPL >= 24 ? 1 : (VPL <= 8 || VPL == 16) ? 3 : 2;
