@@ -75,3 +75,21 @@ def test_precision_names():
     arch = model.Architecture(64, 1, 2, 128)
     with pytest.raises(ValueError):
         B200Network(arch, weights.random_init(arch), precision="fp32")
+
+
+def test_host_entry_points_refuse_a_null_context():
+    """mrn_evaluate and mrn_evaluate_f16 reject a NULL context before any CUDA call, and the
+    message is readable through mrn_last_error(NULL)."""
+    lib = _lib.load()
+    boards = np.zeros((1, _lib.BOARD_BYTES), dtype=np.uint8)
+    legal = np.full((1, _lib.MAX_LEGAL), -1, dtype=np.int32)
+    wdl = np.zeros((1, 3), dtype=np.float32)
+    b = boards.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8))
+    lg = legal.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))
+    w = wdl.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    p32 = np.zeros((1, _lib.MAX_LEGAL), dtype=np.float32)
+    p16 = np.zeros((1, _lib.MAX_LEGAL), dtype=np.float16)
+    assert lib.mrn_evaluate(None, 1, b, lg, p32.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), w) == 1
+    assert b"context is NULL" in lib.mrn_last_error(None)
+    assert lib.mrn_evaluate_f16(None, 1, b, lg, p16.ctypes.data, w) == 1
+    assert b"context is NULL" in lib.mrn_last_error(None)
