@@ -177,16 +177,21 @@ class B200Network(Network):
         self._check(rc, "forward")
         return priors, wdl
 
-    def evaluate_packed_f16(self, boards: np.ndarray, legal: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    def evaluate_packed_f16(self, boards: np.ndarray, legal: np.ndarray, priors: np.ndarray | None = None,
+                            wdl: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:
         """`mrn_evaluate_f16`: as `evaluate_packed`, with the priors returned as float16 [n, 224]
-        (half the bytes copied back from the GPU)."""
+        (half the bytes copied back from the GPU; written into `priors` / `wdl` when given)."""
         boards = np.ascontiguousarray(boards, dtype=np.uint8)
         legal = np.ascontiguousarray(legal, dtype=np.int32)
         n = boards.shape[0]
         if boards.shape != (n, BOARD_BYTES) or legal.shape != (n, MAX_LEGAL):
             raise ValueError("boards must be [n, 66] and legal [n, 224]")
-        priors = np.empty((n, MAX_LEGAL), dtype=np.float16)
-        wdl = np.empty((n, 3), dtype=np.float32)
+        if priors is None:
+            priors = np.empty((n, MAX_LEGAL), dtype=np.float16)
+        if wdl is None:
+            wdl = np.empty((n, 3), dtype=np.float32)
+        if priors.dtype != np.float16 or priors.shape != (n, MAX_LEGAL) or not priors.flags.c_contiguous:
+            raise ValueError("priors must be a C-contiguous float16 [n, 224] array")
         rc = self._lib.mrn_evaluate_f16(self._ctx, n, boards.ctypes.data_as(POINTER(c_uint8)),
                                         legal.ctypes.data_as(POINTER(c_int32)), priors.ctypes.data, _f32p(wdl))
         self._check(rc, "forward")
@@ -287,16 +292,29 @@ class ShardedNetwork(Network):
             raise error if isinstance(error, NetworkError) else NetworkError(str(error))
         return out
 
-    def evaluate_packed(self, boards: np.ndarray, legal: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    def _packed(self, method: str, prior_dtype, boards: np.ndarray, legal: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+        """Packed batches: each replica writes its shard straight into its rows of the outputs."""
         n = boards.shape[0]
-        priors = np.empty((n, MAX_LEGAL), dtype=np.float32)
+        priors = np.empty((n, MAX_LEGAL), dtype=prior_dtype)
         wdl = np.empty((n, 3), dtype=np.float32)
         spans = self.shards(n, len(self.replicas))
-        futures = [self._pool.submit(r.evaluate_packed, boards[a:b], legal[a:b], priors[a:b], wdl[a:b])
+        futures = [self._pool.submit(getattr(r, method), boards[a:b], legal[a:b], priors[a:b], wdl[a:b])
                    for r, (a, b) in zip(self.replicas, spans) if b > a]
+        error = None
         for f in futures:
-            f.result()
+            try:
+                f.result()
+            except Exception as e:  # noqa: BLE001 - re-raised below as the trait's error type
+                error = error or e
+        if error is not None:
+            raise error if isinstance(error, NetworkError) else NetworkError(str(error))
         return priors, wdl
+
+    def evaluate_packed(self, boards: np.ndarray, legal: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+        return self._packed("evaluate_packed", np.float32, boards, legal)
+
+    def evaluate_packed_f16(self, boards: np.ndarray, legal: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+        return self._packed("evaluate_packed_f16", np.float16, boards, legal)
 
     def describe(self) -> str:
         return f"{len(self.replicas)} replicas: " + "; ".join(r.describe() for r in self.replicas)

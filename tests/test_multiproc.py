@@ -60,6 +60,18 @@ class FakeNet(Network):
         return [Evaluation(np.asarray(acts, np.float32) / max(1, sum(acts)), (float(board[0]), 0.0, 0.0))
                 for board, acts in batch]
 
+    def evaluate_packed(self, boards, legal, priors, wdl):
+        self.seen.append((threading.get_ident(), len(boards)))
+        time.sleep(self.delay)
+        if self.fail:
+            raise RuntimeError(f"replica {self.tag} lost its device")
+        priors[:] = np.where(legal >= 0, legal, 0).astype(priors.dtype)
+        wdl[:] = 0.0
+        wdl[:, 0] = boards[:, 0]
+        return priors, wdl
+
+    evaluate_packed_f16 = evaluate_packed
+
     def describe(self):
         return f"fake {self.tag}"
 
@@ -92,3 +104,26 @@ def test_a_failing_replica_fails_the_batch():
         net.evaluate(_leaves(5))
     # the healthy configuration still works afterwards
     assert len(ShardedNetwork([FakeNet(0), FakeNet(1)]).evaluate(_leaves(5))) == 5
+
+
+@pytest.mark.parametrize("method,dtype", [("evaluate_packed", np.float32), ("evaluate_packed_f16", np.float16)])
+def test_sharded_packed_batches_land_in_order(method, dtype):
+    """Packed batches: every replica writes its contiguous shard into its own rows of one output
+    array (f32 or f16 priors), concurrently; a replica's failure fails the batch as NetworkError."""
+    n = 11
+    boards = np.zeros((n, 66), np.uint8)
+    boards[:, 0] = np.arange(n)
+    legal = np.full((n, 224), -1, np.int32)
+    legal[:, :3] = np.arange(3 * n).reshape(n, 3)
+    reps = [FakeNet(i, delay=0.2) for i in range(3)]
+    net = ShardedNetwork(reps)
+    t0 = time.perf_counter()
+    priors, wdl = getattr(net, method)(boards, legal)
+    assert time.perf_counter() - t0 < 0.5  # three 0.2 s shards overlap
+    assert priors.dtype == dtype and priors.shape == (n, 224)
+    assert np.array_equal(priors[:, :3], legal[:, :3].astype(dtype)) and not priors[:, 3:].any()
+    assert np.array_equal(wdl[:, 0], np.arange(n, dtype=np.float32))
+    assert [k for r in reps for _, k in r.seen] == [4, 4, 3]
+    bad = ShardedNetwork([FakeNet(0), FakeNet(1, fail=True)])
+    with pytest.raises(NetworkError, match="replica 1"):
+        getattr(bad, method)(boards, legal)
