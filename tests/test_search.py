@@ -6,6 +6,7 @@ collisions are counted, and the chosen move is legal."""
 import ctypes
 
 import numpy as np
+import pytest
 
 from marina_b200 import chess, search
 
@@ -59,3 +60,30 @@ def test_terminal_root_uses_no_network_slot():
     per_root, _ = search.search([stalemate], 100, [(uniform_net, None)], workers_per_evaluator=1,
                                 params=search.default_params(16))
     assert per_root[0]["network_evals"] == 0 and per_root[0]["nodes"] >= 100 and not calls
+
+
+def _summary_keys(s):
+    return {k: s[k] for k in ("nodes", "network_evals", "batches", "collisions", "max_depth", "tree_nodes",
+                              "best_action", "error")}
+
+
+def test_one_worker_search_is_deterministic():
+    """With one gathering thread and a deterministic network, two searches of the same roots
+    visit the same tree (the reference checks determinism at src/search/mod.rs:1690)."""
+    roots = [chess.startpos(), chess.from_fen("r1bqkbnr/pppp1ppp/2n5/4p3/4P3/5N2/PPPP1PPP/RNBQKB1R w KQkq - 2 3")]
+    runs = [search.search(roots, 1500, [(uniform_net, None)], workers_per_evaluator=1,
+                          params=search.default_params(32))[0] for _ in range(2)]
+    assert [_summary_keys(s) for s in runs[0]] == [_summary_keys(s) for s in runs[1]]
+
+
+@search.EVAL_FN
+def failing_net(ctx, n, boards, legal, priors, wdl):
+    return 6
+
+
+def test_a_network_error_stops_the_search_and_is_reported():
+    """A network call that fails ends the search with that error code, as `NetworkFailed` does
+    in the reference (src/search/mod.rs:794-797); nothing is substituted for the evaluation."""
+    with pytest.raises(RuntimeError, match="network error 6"):
+        search.search([chess.startpos()], 1000, [(failing_net, None)], workers_per_evaluator=1,
+                      params=search.default_params(16))
