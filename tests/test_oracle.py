@@ -83,7 +83,11 @@ def _tiny_arch():
     return model.Architecture(64, 2, 2, 128)
 
 
-@pytest.mark.parametrize("arch_fn,n,threads", [(_tiny_arch, 9, 1), (model.nano, 5, 3)])
+def _tiny_tanh_arch():
+    return model.Architecture(64, 2, 2, 128, gelu=model.GELU_TANH)
+
+
+@pytest.mark.parametrize("arch_fn,n,threads", [(_tiny_arch, 9, 1), (_tiny_tanh_arch, 7, 2), (model.nano, 5, 3)])
 def test_forward_matches_float64_reference(arch_fn, n, threads):
     arch = arch_fn()
     w = weights.random_init(arch, seed=3, std=0.05, bias_std=0.05, norm_std=0.1)
