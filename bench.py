@@ -532,11 +532,12 @@ def run_wholebox(args):
 
 
 def run_gemm(args):
-    """Our tcgen05 GEMM (through mrn_test_gemm) and cuBLASLt FP8 (torch._scaled_mm, e4m3 x e4m3 ->
-    bf16 with a bias) on the encoder's four GEMM shapes at this batch, e4m3 operands. cuBLASLt gets
-    the plain bias epilogue on every shape (its residual would be a bf16 beta=1 add); ours runs the
-    epilogue the forward pass uses (bias->bf16, GELU->e4m3, f16 residual add). CUDA events, after
-    warm-up; inputs > L2."""
+    """Our tcgen05 GEMM (through mrn_test_gemm) beside cuBLAS on the encoder's four GEMM shapes at
+    this batch: with `--precision fp8` e4m3 operands against cuBLASLt FP8 (torch._scaled_mm, e4m3 x
+    e4m3 -> bf16 with a bias), otherwise bf16 operands (kind::f16) against cuBLAS bf16
+    (torch.addmm). cuBLAS gets the plain bias epilogue on every shape (its residual would be a
+    bf16 beta=1 add); ours runs the epilogue the forward pass uses (bias->bf16, GELU->e4m3 or bf16,
+    f16 residual add). CUDA events, after warm-up; inputs > L2."""
     import ctypes
 
     import torch
@@ -546,26 +547,36 @@ def run_gemm(args):
     arch, _ = load_net(args.net)
     d, ff, M = arch.d_model, arch.d_ff, args.batch * 65
     dev = torch.device("cuda", 0)
-    lib = _lib.load()
+    lib = _lib.load_test()
     stream = torch.cuda.current_stream().cuda_stream
     status = torch.zeros(1, dtype=torch.int32, device=dev)
+    fp8 = args.precision == "fp8"
     out = []
     for name, N, K, epi, odt in [("qkv", 3 * d, d, 0, torch.bfloat16), ("out_proj", d, d, 3, torch.float16),
-                                 ("ffn1", ff, d, 2, torch.uint8), ("ffn2", d, ff, 3, torch.float16)]:
-        a = (torch.randn(M, K, device=dev) * 0.5).to(torch.float8_e4m3fn)
-        b = (torch.randn(N, K, device=dev) * 0.5).to(torch.float8_e4m3fn)
+                                 ("ffn1", ff, d, 2 if fp8 else 1, torch.uint8 if fp8 else torch.bfloat16),
+                                 ("ffn2", d, ff, 3, torch.float16)]:
+        if fp8:
+            a = (torch.randn(M, K, device=dev) * 0.5).to(torch.float8_e4m3fn)
+            b = (torch.randn(N, K, device=dev) * 0.5).to(torch.float8_e4m3fn)
+        else:
+            a = (torch.randn(M, K, device=dev) * 0.5).to(torch.bfloat16)
+            b = (torch.randn(N, K, device=dev) * 0.05).to(torch.bfloat16)
         bias = torch.randn(N, device=dev)
         o = torch.zeros(M, N, device=dev, dtype=odt)
 
         def ours():
-            rc = lib.mrn_test_gemm(1, epi, a.data_ptr(), b.data_ptr(), bias.data_ptr(), o.data_ptr(), N, M, N, K,
-                                   1e-3, 10.0, ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(stream))
+            rc = lib.mrn_test_gemm(int(fp8), epi, a.data_ptr(), b.data_ptr(), bias.data_ptr(), o.data_ptr(), N, M, N,
+                                   K, 1e-3 if fp8 else 1.0, 10.0, ctypes.c_void_p(status.data_ptr()),
+                                   ctypes.c_void_p(stream))
             assert rc == 0, lib.mrn_test_last_error().decode()
 
         one, bias16 = torch.tensor(1.0, device=dev), bias.to(torch.bfloat16)
 
         def cublas():
-            torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, bias=bias16, out_dtype=torch.bfloat16)
+            if fp8:
+                torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, bias=bias16, out_dtype=torch.bfloat16)
+            else:
+                torch.addmm(bias16, a, b.t())
 
         row = {"gemm": name, "M": M, "N": N, "K": K}
         for label, fn in (("ours_us", ours), ("cublaslt_us", cublas)):
@@ -583,7 +594,8 @@ def run_gemm(args):
         row["cublaslt_tflops"] = 2 * M * N * K / row["cublaslt_us"] / 1e6
         assert int(status.item()) == 0
         out.append(row)
-    print(json.dumps({"mode": "gemm", "net": args.net, "batch": args.batch, "dtype": "e4m3", "shapes": out}), flush=True)
+    print(json.dumps({"mode": "gemm", "net": args.net, "batch": args.batch, "dtype": "e4m3" if fp8 else "bf16",
+                      "shapes": out}), flush=True)
 
 
 def main():

@@ -12,8 +12,11 @@
  *     (no context yet) are reported by `mrn_last_error(NULL)` on the calling thread.
  *   - The caller owns every host buffer it passes; the library owns the device memory,
  *     pinned staging buffers, streams and CUDA graphs of a context.
- *   - One context per GPU. Calls on one context are serialised inside the library and may
- *     come from any thread (the device is made current on each call).
+ *   - One context per GPU. Calls on one context may come from any thread (the device is made
+ *     current on each call); the library serialises them, and the GPU work of each pass waits
+ *     for the context's previous pass even when the two were enqueued on different streams
+ *     (except while the caller's stream is being captured into a graph, where ordering the
+ *     captured work is the caller's).
  *   - There is no CPU fallback: without a usable sm_100 device `mrn_create` fails.
  */
 #ifndef MARINA_B200_H
@@ -196,58 +199,46 @@ MRN_API const char* mrn_last_error(mrn_ctx* ctx);
 
 MRN_API void mrn_destroy(mrn_ctx* ctx);
 
+/* ---- several GPUs: one weight replica per device, every batch sharded across them */
+typedef struct mrn_group mrn_group;
+
+/* One context per entry of `devices` (a device may be listed more than once), each sized for its
+ * shard of `max_batch` (ceil(max_batch / n_devices) positions), plus one evaluator thread per
+ * device after the first. The reference has no multi-GPU backend (it builds its CUDA network on
+ * ordinal 0, src/net/mod.rs:171-192); this is the sharding wrapper that makes a whole box one
+ * `Network`. Failures are reported by `mrn_group_last_error(NULL)` on the calling thread. */
+MRN_API int mrn_group_create(const mrn_arch* arch, const mrn_weights* weights, const int* devices, int n_devices,
+                             int max_batch, int precision, mrn_group** out);
+
+/* `mrn_evaluate` over the group: the batch is cut into n_devices contiguous shards (sizes differ by
+ * at most one position), evaluated at the same time, one per device, and written into `priors` /
+ * `wdl` at the shard's offset, so the outputs are in input order. No data moves between GPUs.
+ * On failure the message names the device and the shard's positions. */
+MRN_API int mrn_group_evaluate(mrn_group* group, int n, const uint8_t* boards, const int32_t* legal, float* priors,
+                               float* wdl);
+MRN_API int mrn_group_size(mrn_group* group);
+/* The context of the group's i-th device (owned by the group). */
+MRN_API mrn_ctx* mrn_group_context(mrn_group* group, int i);
+MRN_API const char* mrn_group_describe(mrn_group* group);
+/* Message of the last failure on `group`, or of the calling thread's last `mrn_group_create`
+ * when `group` is NULL. Never NULL. */
+MRN_API const char* mrn_group_last_error(mrn_group* group);
+MRN_API void mrn_group_destroy(mrn_group* group);
+
 /* The forward pass of `mrn_evaluate_device` for callers that cannot allocate device memory
  * once running (a host whose device memory belongs to another allocator, a thread that must
  * not stall on an allocation, a device that is already full). It allocates nothing: all
- * intermediate buffers live in one 8 MiB array compiled into the library, resident on every
- * GPU that loads it for the life of the process. Batches are limited to what fits that array
- * (12 positions for the `small` network in bf16/fp8w, 17 in fp8; 33 / 47 for `nano`); larger
- * ones return MRN_ERR_BATCH_TOO_LARGE. Inputs and outputs are the caller's device buffers, as
- * for `mrn_evaluate_device`. Every call on a device shares the array, so calls whose GPU work
- * overlaps (other streams, other contexts on the same device) corrupt each other's results:
- * serialise them. The first call on a device looks the array's address up; make it before any
- * stream capture. This entry point has no counterpart in the reference. */
+ * intermediate buffers live in one 8 MiB array compiled into the library. `mrn_create` looks
+ * the array up on its device (which is when the driver allocates it) and loads every kernel
+ * the pass launches, so the array stays resident on every GPU that has had a context, for the
+ * life of the process. Batches are limited to what fits that array (12 positions for the
+ * `small` network in bf16/fp8w, 17 in fp8; 33 / 47 for `nano`); larger ones return
+ * MRN_ERR_BATCH_TOO_LARGE. Inputs and outputs are the caller's device buffers, as for
+ * `mrn_evaluate_device`. Every call on a device shares the array, so calls whose GPU work
+ * overlaps (through other contexts on the same device) corrupt each other's results: serialise
+ * them. This entry point has no counterpart in the reference. */
 MRN_API int mrn_evaluate_device_static(mrn_ctx* ctx, int n, const uint8_t* d_boards, const int32_t* d_legal,
                                        float* d_priors, float* d_wdl, void* stream);
-
-/* ---- kernel-level entry points for the GPU test-suite (device pointers, caller's stream) */
-
-/* One GEMM launch: out = epilogue(a[m,k] . b[n,k]^T * scale + bias). `fp8` selects e4m3
- * operands; `epilogue` is 0 bias->bf16, 1 GELU->bf16, 2 GELU->e4m3 (x inv_q), 3 residual
- * add into f16 `out` (4, the fused LayerNorm, goes through mrn_test_gemm_ln). */
-MRN_API int mrn_test_gemm(int fp8, int epilogue, const void* a, const void* b, const float* bias, void* out, int ldo, int m,
-                  int n, int k, float scale, float inv_q, int* status, void* stream);
-/* One residual GEMM with the following LayerNorm fused in (the kernel that can serve out-proj ->
- * norm2 and FFN2 -> the next norm1): x[m,d] (f16) += a[m,k] . b[d,k]^T * scale + bias, then
- * h = LN(x) * gamma + beta (eps), as bf16, or with `fp8` (e4m3 operands) as e4m3 codes of
- * h * inv_q. */
-MRN_API int mrn_test_gemm_ln(int fp8, const void* a, const void* b, const float* bias, const float* gamma,
-                             const float* beta, void* x, void* h, int m, int d, int k, float scale, float eps,
-                             float inv_q, int* status, void* stream);
-/* One GEMM whose A operand is the LayerNorm of the f16 rows x[m,k], computed inside the kernel
- * (the kernel that serves norm1 -> QKV and norm2 -> FFN1 for e4m3 operands, k = 512, n a multiple
- * of 256): A = e4m3 codes of (LN(x) * gamma + beta) * a_inv_q (eps), then as mrn_test_gemm with
- * `epilogue` 0 (bias->bf16), 2 (GELU->e4m3) or 6 (tanh GELU->e4m3) on e4m3 `b`. */
-MRN_API int mrn_test_gemm_norm(int epilogue, const void* x, const float* gamma, const float* beta, float eps,
-                               float a_inv_q, const void* b, const float* bias, void* out, int ldo, int m, int n,
-                               int k, float scale, float inv_q, int* status, void* stream);
-/* The encoder's MLP block in one launch (FFN1 -> GELU -> FFN2 -> residual add; the hidden
- * [m, ff] tensor never leaves the chip): x[m,d] (f16) += e4m3(GELU(h . w1^T * s1 + b1) * inv_q)
- * . w2^T * s2 + b2, with e4m3 h [m,d], w1 [ff,d], w2 [d,ff]; `tanh_gelu` selects the tanh form.
- * d = 512, ff a multiple of 256. */
-MRN_API int mrn_test_mlp(int tanh_gelu, const void* h, const void* w1, const float* b1, const void* w2,
-                         const float* b2, void* x, int m, int d, int ff, float s1, float inv_q, float s2, int* status,
-                         void* stream);
-/* The attention kernel on its own: per (position, head), softmax(Q K^T / sqrt(hd)) V over the
- * position's 65 tokens from bf16 qkv [positions*65, 3d] (Q | K | V, head h at columns h*hd) into
- * out [positions*65, d], bf16, or with `e4m3` as e4m3 codes of the value * inv_q. */
-MRN_API int mrn_test_attention(const void* qkv, void* out, int positions, int d, int heads, int e4m3, float inv_q,
-                               int* status, void* stream);
-/* The LayerNorm kernel on its own: out[rows,d] = LN(x) * gamma + beta from f16 x, as bf16, or
- * with `e4m3` as e4m3 codes of the value * inv_q. */
-MRN_API int mrn_test_layernorm(const void* x, const float* gamma, const float* beta, float eps, int e4m3,
-                               float inv_q, void* out, int rows, int d, void* stream);
-MRN_API const char* mrn_test_last_error(void);
 
 #ifdef __cplusplus
 }

@@ -3,6 +3,9 @@ files travel with the source tree:
 
 * ``libmarina_b200.so`` -- the CUDA evaluator (sm_100a only) and its C ABI
   (``include/marina_b200.h``);
+* ``libmarina_b200_test.so`` -- the GPU test-suite's kernel-level entry points
+  (``include/marina_b200_test.h``) over the same kernel sources compiled with ``MRN_TEST_HOOKS``;
+  the evaluator library exports none of them;
 * ``libmarina_chess.so`` -- the host-side position library (move generation, the
   reference's board/action encoding, seeded random playouts; ``include/marina_chess.h``) and
   the batched PUCT search that drives the evaluator for the nodes/s measurement
@@ -25,11 +28,12 @@ CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 
 CUDA_LIB = PKG / "libmarina_b200.so"
+TEST_LIB = PKG / "libmarina_b200_test.so"
 CHESS_LIB = PKG / "libmarina_chess.so"
 
-CUDA_SOURCES = ["gemm.cu", "kernels.cu", "attention.cu", "runtime.cu", "static_forward.cu", "api_test.cu"]
-CUDA_HEADERS = ["ptx.cuh", "rows.cuh", "gemm.cuh", "gemm.h", "gemm_ln.cuh", "gemm_norm.cuh", "gemm_mlp.cuh", "tmap.h",
-                "kernels.cuh", "launch.h", "runtime.h"]
+CUDA_SOURCES = ["gemm.cu", "kernels.cu", "attention.cu", "runtime.cu", "static_forward.cu", "group.cpp"]
+TEST_SOURCES = ["gemm.cu", "kernels.cu", "attention.cu", "api_test.cu"]
+CUDA_HEADERS = ["ptx.cuh", "rows.cuh", "gemm.cuh", "gemm.h", "tmap.h", "kernels.cuh", "launch.h", "runtime.h"]
 CHESS_SOURCES = ["chess.cpp", "puct.cpp"]
 
 NVCC_FLAGS = [
@@ -61,26 +65,37 @@ def _run(cmd: list[str]) -> None:
         raise RuntimeError(f"build failed ({' '.join(cmd[:3])} ...):\n{proc.stdout}")
 
 
-def build_cuda(force: bool = False, verbose: bool = False) -> Path:
-    srcs = [CSRC / s for s in CUDA_SOURCES if (CSRC / s).exists()]
-    deps = srcs + [CSRC / h for h in CUDA_HEADERS] + [INCLUDE / "marina_b200.h", Path(__file__)]
-    if not force and not _stale(CUDA_LIB, deps):
-        return CUDA_LIB
-    objdir = PKG / "_build"
-    objdir.mkdir(exist_ok=True)
+def _build_shared(out: Path, sources: list[str], objdir: Path, extra: list[str], headers: list[Path], force: bool,
+                  verbose: bool) -> Path:
+    srcs = [CSRC / s for s in sources]
+    deps = srcs + headers + [Path(__file__)]
+    if not force and not _stale(out, deps):
+        return out
+    objdir.mkdir(parents=True, exist_ok=True)
     nvcc = _nvcc()
     objs = []
     for s in srcs:
         o = objdir / (s.stem + ".o")
-        flags = list(NVCC_FLAGS) + (["-Xptxas", "-v"] if verbose else [])
-        if force or _stale(o, [s] + deps[len(srcs):]):
+        flags = list(NVCC_FLAGS) + extra + (["-Xptxas", "-v"] if verbose else [])
+        if force or _stale(o, [s] + headers + [Path(__file__)]):
             _run([nvcc, *flags, f"-I{INCLUDE}", "-c", str(s), "-o", str(o)])
         objs.append(str(o))
-    tmp = CUDA_LIB.with_suffix(".so.tmp")
+    tmp = out.with_suffix(".so.tmp")
     _run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", str(tmp), *objs,
           "-cudart", "static", "-Xcompiler", "-fPIC", "-lpthread", "-ldl", "-lrt"])
-    tmp.replace(CUDA_LIB)
-    return CUDA_LIB
+    tmp.replace(out)
+    return out
+
+
+def build_cuda(force: bool = False, verbose: bool = False) -> Path:
+    headers = [CSRC / h for h in CUDA_HEADERS] + [INCLUDE / "marina_b200.h"]
+    return _build_shared(CUDA_LIB, CUDA_SOURCES, PKG / "_build", [], headers, force, verbose)
+
+
+def build_test(force: bool = False, verbose: bool = False) -> Path:
+    headers = [CSRC / h for h in CUDA_HEADERS] + [INCLUDE / "marina_b200.h", INCLUDE / "marina_b200_test.h"]
+    return _build_shared(TEST_LIB, TEST_SOURCES, PKG / "_build" / "test", ["-DMRN_TEST_HOOKS"], headers, force,
+                         verbose)
 
 
 def build_chess(force: bool = False) -> Path:
@@ -98,9 +113,11 @@ def build_chess(force: bool = False) -> Path:
 def build_all(force: bool = False, verbose: bool = False) -> None:
     build_chess(force)
     build_cuda(force, verbose)
+    build_test(force, verbose)
 
 
 if __name__ == "__main__":
     build_all(force="--force" in sys.argv, verbose="-v" in sys.argv)
     print(CUDA_LIB)
+    print(TEST_LIB)
     print(CHESS_LIB)

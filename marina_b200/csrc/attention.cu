@@ -22,7 +22,6 @@
 // is bounded (kWaitLimitNs); a wait that gives up records an error code and the kernel unwinds.
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
-#include <stdlib.h>
 
 #include "kernels.cuh"
 #include "launch.h"
@@ -280,287 +279,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
 }
 
-// ---- tcgen05 attention (head_dim 64) ---------------------------------------------------
-// The same (position, head) items on the fifth-generation tensor cores: per item two MMAs with
-// M = 128 (the 65 query rows of the box, the rest ignored), S = Q K^T (N = 80 keys of the box,
-// K = 64) into TMEM, then O = P V with P (bf16) written back into TMEM by the softmax warps as
-// the MMA's A operand and V read straight from the TMA box as an N-major B operand (N = 64,
-// K = 80). The tensor work per item drops from ~780k mma.sync MACs to 1.3M tcgen05 MACs issued
-// by one thread, so the kernel is left to the HBM traffic of Q, K, V.
-//
-// Roles: warp 0 lane 0 TMA producer (Q, K, V boxes into kTcSmemSlots item buffers); warp 1 lane 0
-// MMA issuer; warps 2.. in kTcGroups groups of four, one query row per thread (warp w: TMEM lanes
-// 32 (w % 4)): group g runs softmax and epilogue of the items k = g mod kTcGroups, each in its own
-// TMEM slot of 128 columns (S in [0, 80), then P in [0, 40) and O in [40, 104)). Per item:
-// MMA1(k) | softmax(k) | MMA2(k) | epilogue(k); the groups keep kTcGroups items in flight and the
-// MMA issuer polls both queues and issues whichever is ready. Every wait is bounded.
-constexpr int kTcSmemSlots = 6;
-constexpr int kTcGroups = 4;
-constexpr int kTcTmemSlots = kTcGroups;  // one per softmax group
-constexpr int kTcTmemStride = 128;
-constexpr int kTcKeys = kAttnRows;  // N of S = Q K^T, K of O = P V
-constexpr int kTcThreads = 32 * (2 + 4 * kTcGroups);
-
-template <bool E4M3>
-__global__ void __launch_bounds__(kTcThreads, 1)
-    attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, AttentionParams p, int items) {
-  constexpr int HD = 64, T = 65;
-  constexpr int RB = HD * 2;
-  constexpr int MAT = kAttnRows * RB;  // 10 KB: one of Q, K, V
-  constexpr int ITEM = 3 * MAT;
-  constexpr uint32_t kIdescS = idesc_bf16(128, kTcKeys);
-  constexpr uint32_t kIdescO = idesc_bf16_bmn(128, HD);
-  constexpr uint32_t kPCol = 0, kOCol = kTcKeys / 2;  // P over S's first 40 columns, O after it
-  static_assert(kOCol + HD <= kTcTmemStride && kTcTmemSlots * kTcTmemStride <= 512, "TMEM columns");
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTcSmemSlots * ITEM);  // [kTcSmemSlots]
-  uint64_t* sfree = full + kTcSmemSlots;                                      // [kTcSmemSlots]
-  uint64_t* s_full = sfree + kTcSmemSlots;                                    // [kTcTmemSlots]
-  uint64_t* p_full = s_full + kTcTmemSlots;
-  uint64_t* o_full = p_full + kTcTmemSlots;
-  uint64_t* t_free = o_full + kTcTmemSlots;
-  uint64_t* drain = t_free + kTcTmemSlots;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int d = p.d, heads = p.heads;
-  const int G = static_cast<int>(gridDim.x);
-  const int mine = (items - static_cast<int>(blockIdx.x) + G - 1) / G;  // this CTA's items
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kTcSmemSlots; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&sfree[i], 1);
-    }
-    for (int i = 0; i < kTcTmemSlots; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&t_free[i], 4);
-    }
-    mbar_init(drain, 1);
-    *abort = 0;
-    fence_barrier_init();
-    tma_prefetch_map(&map_qkv);
-  }
-  if (warp == 0) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  grid_dep_wait();
-  grid_dep_launch();
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ---- producer
-      uint32_t issued = 0, parities = 0;
-      for (int k = 0; k < mine && !*abort; ++k) {
-        const int item = static_cast<int>(blockIdx.x) + k * G;
-        const int sl = k % kTcSmemSlots;
-        const uint32_t par = (k / kTcSmemSlots) & 1;
-        if (!mbar_wait(&sfree[sl], par ^ 1u, abort)) {
-          raise_error(p.status, abort, kErrTimeoutAttention);
-          break;
-        }
-        const int pos = item / heads, head = item - pos * heads;
-        uint8_t* dst = smem + sl * ITEM;
-        mbar_arrive_expect_tx(&full[sl], ITEM);
-        tma_load_2d(dst, &map_qkv, &full[sl], head * HD, pos * T);
-        tma_load_2d(dst + MAT, &map_qkv, &full[sl], d + head * HD, pos * T);
-        tma_load_2d(dst + 2 * MAT, &map_qkv, &full[sl], 2 * d + head * HD, pos * T);
-        issued |= 1u << sl;
-        parities = (parities & ~(1u << sl)) | (par << sl);
-      }
-      if (*abort) {
-        for (int sl = 0; sl < kTcSmemSlots; ++sl)
-          if (issued & (1u << sl)) mbar_wait_bounded(&full[sl], (parities >> sl) & 1u);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ---- MMA issuer, event-driven: MMA1 of the next item as soon as its Q/K/V have landed and
-      // its TMEM slot is free (at most kTcGroups items ahead), MMA2 of the oldest item as soon
-      // as its P is in TMEM; both in item order.
-      bool issued = false;
-      int n1 = 0, n2 = 0;
-      unsigned long long idle_since = 0;
-      uint32_t spins = 0;
-      while (n2 < mine) {
-        bool progress = false;
-        if (n1 < mine && n1 - n2 < kTcGroups) {
-          const int t = n1 % kTcTmemSlots, sl = n1 % kTcSmemSlots;
-          if (mbar_test(smem_u32(&full[sl]), (n1 / kTcSmemSlots) & 1u) &&
-              mbar_test(smem_u32(&t_free[t]), ((n1 / kTcTmemSlots) & 1u) ^ 1u)) {
-            tc_fence_after();
-            const uint32_t q = smem_u32(smem + sl * ITEM), kb = q + MAT;
-            // Q rows 80..127 run into the K box: garbage query rows, never read back.
-#pragma unroll
-            for (int kk = 0; kk < HD / 16; ++kk)
-              mma_bf16(tmem + static_cast<uint32_t>(t * kTcTmemStride), desc_sw128(q + 32u * kk),
-                       desc_sw128(kb + 32u * kk), kIdescS, kk != 0);
-            issued = true;
-            tc_commit(&s_full[t]);
-            ++n1;
-            progress = true;
-          }
-        }
-        if (n2 < n1) {
-          const int t = n2 % kTcTmemSlots, sl = n2 % kTcSmemSlots;
-          if (mbar_test(smem_u32(&p_full[t]), (n2 / kTcTmemSlots) & 1u)) {
-            tc_fence_after();
-            const uint32_t base = tmem + static_cast<uint32_t>(t * kTcTmemStride);
-            const uint32_t v = smem_u32(smem + sl * ITEM + 2 * MAT);
-#pragma unroll
-            for (int kk = 0; kk < kTcKeys / 16; ++kk)  // 16 keys = 8 P columns = 16 V rows (2048 B)
-              mma_bf16_tmem_a(base + kOCol, base + kPCol + 8u * kk, desc_sw128(v + 2048u * kk), kIdescO, kk != 0);
-            tc_commit(&o_full[t]);
-            tc_commit(&sfree[sl]);
-            ++n2;
-            progress = true;
-          }
-        }
-        if (progress) {
-          spins = 0;
-        } else if ((++spins & 31u) == 0) {
-          const unsigned long long now = globaltimer();
-          if (idle_since == 0) idle_since = now;
-          if (*abort || now - idle_since > kWaitLimitNs) {
-            raise_error(p.status, abort, kErrTimeoutAttention);
-            break;
-          }
-        }
-        if (progress) idle_since = 0;
-      }
-      if (*abort && issued) {
-        tc_commit(drain);
-        if (!mbar_wait_bounded(drain, 0) && p.status) atomicCAS(p.status, 0, kErrTimeoutDrain);
-      }
-    }
-  } else {
-    // ---- softmax + epilogue: one query row per thread, group g takes items g, g + kTcGroups, ...
-    const int group = (warp - 2) >> 2;
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const bool valid = row < T;
-    const uint32_t lanes = static_cast<uint32_t>(quarter * 32) << 16;
-    const float scale_log2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) in base 2
-    for (int k = group; k < mine; k += kTcGroups) {
-      const int t = k % kTcTmemSlots;
-      const uint32_t par = (k / kTcTmemSlots) & 1u;
-      const uint32_t base = tmem + lanes + static_cast<uint32_t>(t * kTcTmemStride);
-      if (!mbar_wait(&s_full[t], par, abort)) {
-        if (lane == 0) raise_error(p.status, abort, kErrTimeoutAttention);
-        break;
-      }
-      tc_fence_after();
-      if (quarter == 3) {
-        // Query rows 96..127 do not exist: keep in step with the group's barriers, nothing else
-        // (MMA2 multiplies whatever these TMEM lanes hold into output rows that are never read).
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[t]);
-        if (!mbar_wait(&o_full[t], par, abort)) {
-          if (lane == 0) raise_error(p.status, abort, kErrTimeoutAttention);
-          break;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&t_free[t]);
-        continue;
-      }
-      float sv[80];
-      tmem_ld32(base, *reinterpret_cast<float(*)[32]>(sv));
-      tmem_ld32(base + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
-      tmem_ld16(base + 64, *reinterpret_cast<float(*)[16]>(sv + 64));
-      // Softmax over keys 0..64 (keys 65..79 of the box belong to the next position: P = 0).
-      float m = sv[0];
-#pragma unroll
-      for (int j = 1; j < T; ++j) m = fmaxf(m, sv[j]);
-      const float bm = -m * scale_log2;
-      float l = 0.f;
-      uint32_t pk[40];
-#pragma unroll
-      for (int j = 0; j < 40; ++j) {
-        const float e0 = 2 * j < T ? ex2f(fmaf(sv[2 * j], scale_log2, bm)) : 0.f;
-        const float e1 = 2 * j + 1 < T ? ex2f(fmaf(sv[2 * j + 1], scale_log2, bm)) : 0.f;
-        l += e0 + e1;
-        pk[j] = valid ? pack_bf16(e0, e1) : 0u;
-      }
-#pragma unroll
-      for (int j = 0; j < 40; j += 8) tmem_st8(base + kPCol + j, *reinterpret_cast<const uint32_t(*)[8]>(pk + j));
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
-
-      // epilogue: O row * (1 / l), quantised, 64 contiguous output bytes per row
-      if (!mbar_wait(&o_full[t], par, abort)) {
-        if (lane == 0) raise_error(p.status, abort, kErrTimeoutAttention);
-        break;
-      }
-      tc_fence_after();
-      float o[64];
-      tmem_ld32(base + kOCol, *reinterpret_cast<float(*)[32]>(o));
-      tmem_ld32(base + kOCol + 32, *reinterpret_cast<float(*)[32]>(o + 32));
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&t_free[t]);
-      if (valid) {
-        const int item = static_cast<int>(blockIdx.x) + k * G;
-        const int pos = item / heads, head = item - pos * heads;
-        const float f = (E4M3 ? p.inv_q : 1.f) / l;
-        uint8_t* dst = static_cast<uint8_t*>(p.out) +
-                       ((static_cast<size_t>(pos) * T + row) * d + head * HD) * (E4M3 ? 1 : 2);
-        if constexpr (E4M3) {
-#pragma unroll
-          for (int c = 0; c < 64; c += 16) {
-            __nv_fp8x2_storage_t q8[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              q8[e] = __nv_cvt_float2_to_fp8x2(make_float2(o[c + 2 * e] * f, o[c + 2 * e + 1] * f), __NV_SATFINITE,
-                                               __NV_E4M3);
-            *reinterpret_cast<uint4*>(dst + c) = *reinterpret_cast<const uint4*>(q8);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 64; c += 8) {
-            uint32_t b[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) b[e] = pack_bf16(o[c + 2 * e] * f, o[c + 2 * e + 1] * f);
-            *reinterpret_cast<uint4*>(dst + 2 * c) = make_uint4(b[0], b[1], b[2], b[3]);
-          }
-        }
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-constexpr int attention_tc_smem() {
-  return 1024 + kTcSmemSlots * 3 * kAttnRows * 128 + (2 * kTcSmemSlots + 4 * kTcTmemSlots + 1) * 8 + 16;
-}
-
-// The tcgen05 kernel is opt-in (MRN_ATTN_TC=1): correct, but about 5% slower than the mma.sync
-// kernel at batch 4096 (211 against 200 us per launch); its nine small MMAs per item are bound by
-// per-instruction cost rather than by tensor throughput.
-bool attention_tc_enabled() {
-  static const bool on = [] {
-    const char* e = getenv("MRN_ATTN_TC");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
-
 template <int HD, int T>
 constexpr int attention_smem() {
   return 1024 + kTeams * kBufs * 3 * kAttnRows * HD * 2 + 2 * kTeams * kBufs * 8 + 16;
@@ -609,13 +327,6 @@ cudaError_t launch_attention(const AttentionParams& p, int positions, int head_d
   if (!make_qkv_map(&map, p.qkv, positions * p.t, p.d, head_dim)) return cudaErrorInvalidValue;
   const int items = positions * p.heads;
   const int grid = items < sms ? items : sms;
-  if (head_dim == 64 && attention_tc_enabled()) {
-    if (p.out_type == ActType::kE4m3)
-      return launch_kernel(attention_tc_kernel<true>, dim3(grid), dim3(kTcThreads), attention_tc_smem(), s, map, p,
-                           items);
-    return launch_kernel(attention_tc_kernel<false>, dim3(grid), dim3(kTcThreads), attention_tc_smem(), s, map, p,
-                         items);
-  }
   if (head_dim == 64) return launch_attention_t<64, 65>(p, map, grid, items, s);
   return launch_attention_t<32, 65>(p, map, grid, items, s);
 }
@@ -623,12 +334,6 @@ cudaError_t launch_attention(const AttentionParams& p, int positions, int head_d
 cudaError_t prepare_attention() {
   cudaError_t e = prepare_attention_t<64, 65>();
   if (e != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(attention_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                attention_tc_smem())) != cudaSuccess)
-    return e;
-  if ((e = cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                attention_tc_smem())) != cudaSuccess)
-    return e;
   return prepare_attention_t<32, 65>();
 }
 

@@ -377,7 +377,12 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = 0, parity_mask = 0;  // per stage: a load was issued, and in which phase
-      for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x) {
+#ifdef MRN_TEST_HOOKS
+      const int first_tile = g_test_no_loads ? total : static_cast<int>(blockIdx.x);
+#else
+      const int first_tile = blockIdx.x;
+#endif
+      for (int tile = first_tile; tile < total && !*abort; tile += gridDim.x) {
         const int m0 = (tile / n_tiles) * kTileM;
         const int n0 = (tile % n_tiles) * BN;
         for (int kb = 0; kb < k_blocks; ++kb) {

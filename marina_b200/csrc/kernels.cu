@@ -337,7 +337,25 @@ __global__ void __launch_bounds__(256) priors_to_half_kernel(const float* __rest
   reinterpret_cast<uint2*>(out)[i] = *reinterpret_cast<const uint2*>(h);
 }
 
+// Loads the kernels a network of width d launches (cudaFuncGetAttributes makes the runtime load a
+// function that lazy module loading would otherwise load, and allocate device memory for, at its
+// first launch).
+template <int VPL, int VEC>
+struct LoadKernels {
+  static cudaError_t run(int) {
+    cudaFuncAttributes a;
+    cudaError_t e;
+    if ((e = cudaFuncGetAttributes(&a, embed_ln_kernel<VPL, VEC>)) != cudaSuccess) return e;
+    if ((e = cudaFuncGetAttributes(&a, layernorm_kernel<VPL, VEC>)) != cudaSuccess) return e;
+    if ((e = cudaFuncGetAttributes(&a, heads_kernel<VPL, VEC>)) != cudaSuccess) return e;
+    if ((e = cudaFuncGetAttributes(&a, value_out_kernel<VPL, VEC>)) != cudaSuccess) return e;
+    return cudaFuncGetAttributes(&a, priors_to_half_kernel);
+  }
+};
+
 }  // namespace
+
+cudaError_t load_row_kernels(int d) { return dispatch_d<LoadKernels>(d); }
 
 cudaError_t launch_embed_ln(const EmbedParams& e, const NormParams& n, int positions, int d, cudaStream_t s) {
   return dispatch_d<EmbedLaunch>(d, e, n, positions, s);

@@ -86,6 +86,10 @@ cudaError_t launch_value_out(const ValueOutParams& p, int positions, int d, cuda
 // 16-byte aligned: the priors in half precision for the host copy.
 cudaError_t launch_priors_to_half(const float* in, __half* out, int count, cudaStream_t s);
 
+// Loads (and so allocates the code of) every kernel above for width d, so that no later launch
+// does it.
+cudaError_t load_row_kernels(int d);
+
 // Device error codes raised by these kernels (the GEMM uses 1..4).
 constexpr int kErrBadAction = 16;
 

@@ -16,6 +16,18 @@ namespace mrn {
 // A wait that has not completed after this long is treated as a device-side fault.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
+#ifdef MRN_TEST_HOOKS
+// Test builds only (libmarina_b200_test.so): the limit is a device variable a test can shorten,
+// and the GEMM's TMA producer can be told to issue no loads, so that a test can make a bounded
+// wait run out without any copy or MMA in flight. Each translation unit has its own copy; the
+// GEMM's are set through gemm_test_hooks (gemm.cu).
+static __device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
+static __device__ int g_test_no_loads = 0;
+__device__ __forceinline__ unsigned long long wait_limit_ns() { return *(volatile unsigned long long*)&g_wait_limit_ns; }
+#else
+__device__ __forceinline__ unsigned long long wait_limit_ns() { return kWaitLimitNs; }
+#endif
+
 // Error codes written to the context's status word (first writer wins).
 enum DeviceError : int {
   kErrNone = 0,
@@ -82,43 +94,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Non-blocking probe: has the phase with parity `parity` of `bar` completed? (try_wait may park
-// the thread for a while; a role that polls several barriers uses this.)
-__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
 // Wait until the phase with parity `parity` of `bar` has completed. Gives up (returns
-// false) when `abort` is raised by another role of the CTA or after kWaitLimitNs; the
+// false) when `abort` is raised by another role of the CTA or after wait_limit_ns(); the
 // caller then raises `abort` itself and unwinds.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
-  const unsigned long long start = globaltimer();
+  const unsigned long long start = globaltimer(), limit = wait_limit_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(a, parity)) return true;
     if ((i & 31u) == 0) {
       if (*abort) return false;
-      if (globaltimer() - start > kWaitLimitNs) return false;
+      if (globaltimer() - start > limit) return false;
     }
   }
 }
 
 // The same wait without the abort check, for unwinding after an abort: gives up after
-// kWaitLimitNs.
+// wait_limit_ns().
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
-  const unsigned long long start = globaltimer();
+  const unsigned long long start = globaltimer(), limit = wait_limit_ns();
   while (!mbar_try_wait(a, parity))
-    if (globaltimer() - start > kWaitLimitNs) return false;
+    if (globaltimer() - start > limit) return false;
   return true;
 }
 
@@ -220,18 +218,6 @@ __device__ __forceinline__ void mma_bf16(uint32_t d, uint64_t a, uint64_t b, uin
       : "memory");
 }
 
-// D[tmem] (+)= A[tmem] * B[smem]^T, bf16 x bf16 -> f32: A (M rows, one per TMEM lane, two bf16
-// of K per 32-bit column) is read from tensor memory.
-__device__ __forceinline__ void mma_bf16_tmem_a(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
-                                                uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 // D[tmem] (+)= A[smem] * B[smem]^T, e4m3 x e4m3 -> f32.
 __device__ __forceinline__ void mma_e4m3(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -265,33 +251,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Store 8 consecutive 32-bit TMEM columns of this thread's lane (32x32b shape, the warp's lane
-// quarter), a .sync.aligned warp instruction like the loads. Completion: tmem_wait_st.
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
-  __syncwarp();
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
-      "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// The same for 16 consecutive columns.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  __syncwarp();
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 // ---- CTA pairs (cluster of 2) for tcgen05 cta_group::2 ------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -314,67 +273,6 @@ __device__ __forceinline__ void cluster_sync() {
 // Arrive on an mbarrier in another CTA of the cluster (address from map_to_rank).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-// This CTA's cluster index, the number of clusters in the grid, and CTAs per cluster.
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_count_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_size() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
-  return r;
-}
-
-// Store one f32 into the shared memory of a CTA of the cluster (address from map_to_rank).
-__device__ __forceinline__ void st_cluster_f32(uint32_t cluster_addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
-}
-
-__device__ __forceinline__ void st_cluster_f32x2(uint32_t cluster_addr, float a, float b) {
-  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(cluster_addr), "f"(a), "f"(b) : "memory");
-}
-
-// Orders this thread's earlier shared::cluster stores before its later release operations as
-// seen from every CTA of the cluster.
-__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
-
-// Bounded wait on a local mbarrier whose arrivals come from other CTAs of the cluster
-// (acquire at cluster scope, so their stores before arriving are visible afterwards).
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, const volatile int* abort) {
-  const uint32_t a = smem_u32(bar);
-  if (mbar_try_wait_cluster(a, parity)) return true;
-  const unsigned long long start = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait_cluster(a, parity)) return true;
-    if ((i & 31u) == 0) {
-      if (*abort) return false;
-      if (globaltimer() - start > kWaitLimitNs) return false;
-    }
-  }
-}
-
-// Named barrier over `threads` threads (a multiple of 32) of this CTA; id 0 is __syncthreads.
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // TMA tile load into this CTA's shared memory whose completion bytes are counted on the
@@ -428,42 +326,6 @@ __device__ __forceinline__ void mma_pair_e4m3(uint32_t d, uint64_t a, uint64_t b
       : "memory");
 }
 
-// Arrive on the mbarrier at this shared-memory offset in every CTA of `cta_mask` once the
-// (single-CTA) MMAs issued so far by this thread have completed.
-__device__ __forceinline__ void tc_commit_mc(uint64_t* bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"(cta_mask)
-      : "memory");
-}
-
-// Copy `bytes` (a multiple of 16) of this CTA's shared memory to another CTA of the cluster
-// (`dst_cluster`, `bar_cluster`: addresses from map_to_rank); completion is counted as
-// transaction bytes on that CTA's mbarrier.
-__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, const void* src, uint32_t bytes,
-                                                  uint32_t bar_cluster) {
-  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   dst_cluster),
-               "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
-               : "memory");
-}
-
-// Arrive on an mbarrier of another CTA of the cluster and add `bytes` to its expected
-// transaction count (address from map_to_rank).
-__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t cluster_addr, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_addr),
-               "r"(bytes)
-               : "memory");
-}
-
-// Pull a 2-D tile of a tensor map into L2 (no shared memory, no completion).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA with 128-byte
 // swizzling: rows of 128 bytes, 8-row (1024-byte) swizzle atoms packed densely, so the
 // stride between 8-row groups is 1024 bytes. The tile base must be 1024-byte aligned;
@@ -484,8 +346,6 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
 }
-// kind::f16 bf16 with B given N-major (MN-major: N contiguous in shared memory, K across rows).
-__host__ __device__ constexpr uint32_t idesc_bf16_bmn(int m, int n) { return idesc_bf16(m, n) | (1u << 16); }
 __host__ __device__ constexpr uint32_t idesc_e4m3(int m, int n) {
   return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);

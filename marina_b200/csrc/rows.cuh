@@ -1,6 +1,6 @@
 // Rows of d values held by one warp, and the LayerNorm arithmetic on them: shared by the
-// embedding, LayerNorm and heads kernels and by the GEMM whose A operand is normalised in
-// the kernel (gemm_norm.cuh), so that every LayerNorm of the evaluator rounds the same way.
+// embedding, LayerNorm and heads kernels, so that every LayerNorm of the evaluator rounds the
+// same way.
 #pragma once
 
 #include <cuda_bf16.h>

@@ -241,14 +241,6 @@ int alloc_buffers(mrn_ctx* c) {
 
 namespace mrn {
 
-bool ln_fusion_enabled() {
-  static const bool on = [] {
-    const char* e = getenv("MRN_GEMM_LN");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
-
 // Programmatic dependent launch between the kernels of a pass. MRN_PDL=1: always; MRN_PDL=0:
 // never; unset: for batches of up to kPdlMaxPositions positions. Measured on B200 (small net,
 // e4m3): it takes 13% off the latency of a 1-position pass (0.490 -> 0.425 ms), 8-10% at 16-64
@@ -265,36 +257,6 @@ bool pdl_enabled(int positions) {
   return mode == 1 || (mode == -1 && positions <= kPdlMaxPositions);
 }
 
-bool mlp_enabled() {
-  static const bool on = [] {
-    const char* e = getenv("MRN_MLP");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
-
-bool mlp_args(const GemmArgs& f1, const GemmArgs& f2, MlpArgs* out) {
-  if (!f1.fp8 || !f2.fp8 || f1.norm_x || f2.epi != Epilogue::kResidual ||
-      (f1.epi != Epilogue::kGeluE4m3 && f1.epi != Epilogue::kGeluTanhE4m3))
-    return false;
-  MlpArgs a;
-  a.h = f1.a, a.w1 = f1.b, a.w2 = f2.b, a.b1 = f1.bias, a.b2 = f2.bias, a.x = f2.out;
-  a.m = f1.m, a.d = f1.k, a.ff = f1.n, a.s1 = f1.scale, a.s2 = f2.scale, a.inv_q = f1.inv_q;
-  a.tanh_gelu = f1.epi == Epilogue::kGeluTanhE4m3;
-  a.status = f1.status;
-  if (f2.k != a.ff || f2.n != a.d || f2.ldo != a.d || f1.ldo != a.ff || !mlp_supported(a)) return false;
-  *out = a;
-  return true;
-}
-
-bool norm_a_enabled() {
-  static const bool on = [] {
-    const char* e = getenv("MRN_GEMM_NORM");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
-
 namespace {
 
 GemmArgs base_args(const mrn_ctx* c, int rows) {
@@ -302,8 +264,6 @@ GemmArgs base_args(const mrn_ctx* c, int rows) {
   a.m = rows;
   a.fp8 = c->precision == MRN_PRECISION_FP8;
   a.status = c->status;
-  a.eps = c->eps;
-  a.ln_e4m3 = a.fp8;
   return a;
 }
 
@@ -311,60 +271,28 @@ float gemm_scale(const mrn_ctx* c, const DevLayer& D, int i) {
   return c->precision == MRN_PRECISION_FP8 ? D.ws[i] * D.as[i] : D.ws[i];
 }
 
-// A normalised in the kernel from x with (gamma, beta) and the activation scale of the norm's
-// output, kept only where the normalised-A kernel supports the GEMM.
-void try_norm(GemmArgs& g, const LayerBuffers& b, const float* gamma, const float* beta, float act_scale) {
-  GemmArgs n = g;
-  n.norm_x = b.x, n.gamma = gamma, n.beta = beta, n.ln_inv_q = 1.f / act_scale;
-  if (gemm_norm_supported(n)) g = n;
-}
-
-// QKV: h (or norm1(x)) -> qkv (bf16)
-void qkv_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool norm, GemmArgs& g) {
-  const DevLayer& D = c->dl[l];
-  g = base_args(c, rows);
-  g.a = b.h, g.b = D.w_qkv, g.n = 3 * c->d, g.k = c->d, g.epi = Epilogue::kBias, g.out = b.qkv;
-  g.ldo = 3 * c->d, g.bias = D.b_qkv, g.scale = gemm_scale(c, D, 0);
-  if (norm) try_norm(g, b, D.n1g, D.n1b, D.as[0]);
-}
-
 }  // namespace
 
-bool qkv_normalises(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool norm) {
-  GemmArgs g;
-  qkv_args(c, l, rows, b, norm, g);
-  return g.norm_x != nullptr;
-}
-
-void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool fuse, bool norm, bool mlp,
-                     GemmArgs (&g)[4]) {
+void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, GemmArgs (&g)[4]) {
   const int d = c->d, ff = c->dff;
   const bool fp8 = c->precision == MRN_PRECISION_FP8;
   const DevLayer& D = c->dl[l];
-  qkv_args(c, l, rows, b, norm, g[0]);
-  for (int i = 1; i < 4; ++i) g[i] = base_args(c, rows);
-  // FFN1: h (or norm2(x)) -> ff = GELU(.), the card's form (the value head's GELU is always the erf one)
+  for (int i = 0; i < 4; ++i) g[i] = base_args(c, rows);
+  // QKV: h -> qkv (bf16)
+  g[0].a = b.h, g[0].b = D.w_qkv, g[0].n = 3 * d, g[0].k = d, g[0].epi = Epilogue::kBias, g[0].out = b.qkv;
+  g[0].ldo = 3 * d, g[0].bias = D.b_qkv, g[0].scale = gemm_scale(c, D, 0);
+  // out-proj: attn -> x +=
+  g[1].a = b.attn, g[1].b = D.w_o, g[1].n = d, g[1].k = d, g[1].epi = Epilogue::kResidual, g[1].out = b.x;
+  g[1].ldo = d, g[1].bias = D.b_o, g[1].scale = gemm_scale(c, D, 1);
+  // FFN1: h -> ff = GELU(.), the card's form (the value head's GELU is always the erf one)
   const bool tanh_form = c->gelu == MRN_GELU_TANH;
   g[2].a = b.h, g[2].b = D.w_1, g[2].n = ff, g[2].k = d;
   g[2].epi = fp8 ? (tanh_form ? Epilogue::kGeluTanhE4m3 : Epilogue::kGeluE4m3)
                  : (tanh_form ? Epilogue::kGeluTanhBf16 : Epilogue::kGeluBf16);
   g[2].out = b.ff, g[2].ldo = ff, g[2].bias = D.b_1, g[2].scale = gemm_scale(c, D, 2), g[2].inv_q = 1.f / D.as[3];
-  if (norm && !mlp) try_norm(g[2], b, D.n2g, D.n2b, D.as[2]);
-  // out-proj: attn -> x += (then h = norm2(x), unless FFN1 normalises x itself)
-  g[1].a = b.attn, g[1].b = D.w_o, g[1].n = d, g[1].k = d, g[1].epi = Epilogue::kResidual, g[1].out = b.x;
-  g[1].ldo = d, g[1].bias = D.b_o, g[1].scale = gemm_scale(c, D, 1);
-  if (fuse && !g[2].norm_x) {
-    g[1].epi = Epilogue::kResidualLn, g[1].gamma = D.n2g, g[1].beta = D.n2b, g[1].ln_out = b.h;
-    g[1].ln_inv_q = 1.f / D.as[2];
-  }
-  // FFN2: ff -> x += (then h = norm1 of the next layer, unless its QKV normalises x itself)
+  // FFN2: ff -> x +=
   g[3].a = b.ff, g[3].b = D.w_2, g[3].n = d, g[3].k = ff, g[3].epi = Epilogue::kResidual, g[3].out = b.x;
   g[3].ldo = d, g[3].bias = D.b_2, g[3].scale = gemm_scale(c, D, 3);
-  if (fuse && !mlp && l + 1 < c->layers && !qkv_normalises(c, l + 1, rows, b, norm)) {
-    const DevLayer& N = c->dl[l + 1];
-    g[3].epi = Epilogue::kResidualLn, g[3].gamma = N.n1g, g[3].beta = N.n1b, g[3].ln_out = b.h;
-    g[3].ln_inv_q = 1.f / N.as[0];
-  }
 }
 
 cudaError_t launch_site_layernorm(const mrn_ctx* c, int l, int site, const LayerBuffers& b, int rows,
@@ -375,56 +303,42 @@ cudaError_t launch_site_layernorm(const mrn_ctx* c, int l, int site, const Layer
   return launch_layernorm(b.x, np, rows, c->d, s);
 }
 
+int begin_pass(mrn_ctx* c, cudaStream_t s) {
+  if (!c->pass_recorded || s == c->pass_stream) return MRN_OK;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  CK(cudaStreamIsCapturing(s, &cap));
+  if (cap != cudaStreamCaptureStatusNone) return MRN_OK;
+  CK(cudaStreamWaitEvent(s, c->pass_done, 0));
+  return MRN_OK;
+}
+
+int end_pass(mrn_ctx* c, cudaStream_t s) {
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  CK(cudaStreamIsCapturing(s, &cap));
+  if (cap != cudaStreamCaptureStatusNone) return MRN_OK;
+  CK(cudaEventRecord(c->pass_done, s));
+  c->pass_stream = s;
+  c->pass_recorded = true;
+  return MRN_OK;
+}
+
 }  // namespace mrn
 
 namespace {
 
-// GEMM plans of one bucket: per layer QKV, out-proj, FFN1, FFN2; then value ff1. A residual GEMM
-// whose fused LayerNorm cannot be planned on this device falls back to the plain residual
-// epilogue followed by a LayerNorm launch; where the consuming GEMM normalises x itself, no
-// LayerNorm launch is needed at all.
+// GEMM plans of one bucket: per layer QKV, out-proj, FFN1, FFN2; then value ff1.
 int make_plans(mrn_ctx* c, Bucket& b) {
-  const int M = b.positions * c->t, d = c->d, L = c->layers;
+  const int M = b.positions * c->t, d = c->d;
   char err[256];
   const mrn::LayerBuffers bufs{c->h, c->qkv, c->attn, c->ff, c->x};
-  const bool fuse = mrn::ln_fusion_enabled(), norm = mrn::norm_a_enabled();
-  b.ln_launch.assign(2 * L, 0);
-  b.embed_norm = !mrn::qkv_normalises(c, 0, M, bufs, norm);
-  // The fused MLP where the switch is on and every layer supports it.
-  bool mlp = mrn::mlp_enabled();
-  for (int l = 0; l < L && mlp; ++l) {
+  for (int l = 0; l < c->layers; ++l) {
     GemmArgs g[4];
-    mrn::MlpArgs a;
-    mrn::layer_gemm_args(c, l, M, bufs, fuse, norm, true, g);
-    mlp = mrn::mlp_args(g[2], g[3], &a);
-  }
-  b.mlp.clear();
-  for (int l = 0; l < L; ++l) {
-    GemmArgs g[4];
-    mrn::layer_gemm_args(c, l, M, bufs, fuse, norm, mlp, g);
-    if (mlp) {
-      mrn::MlpArgs a;
-      mrn::MlpPlan mp;
-      mrn::mlp_args(g[2], g[3], &a);
-      if (!mrn::mlp_plan(&mp, a, c->num_sms, err)) return c->fail(MRN_ERR_UNSUPPORTED, "layer %d: %s", l, err);
-      b.mlp.push_back(mp);
-    }
-    bool ln_in_epilogue[2] = {false, false};
+    mrn::layer_gemm_args(c, l, M, bufs, g);
     for (int i = 0; i < 4; ++i) {
       GemmPlan p;
-      if (g[i].epi == Epilogue::kResidualLn) {
-        if (mrn::gemm_plan(&p, g[i], c->num_sms, err)) {
-          ln_in_epilogue[i == 1 ? 0 : 1] = true;
-          b.plans.push_back(p);
-          continue;
-        }
-        g[i].epi = Epilogue::kResidual;
-      }
       if (!mrn::gemm_plan(&p, g[i], c->num_sms, err)) return c->fail(MRN_ERR_UNSUPPORTED, "layer %d: %s", l, err);
       b.plans.push_back(p);
     }
-    b.ln_launch[2 * l] = !ln_in_epilogue[0] && !g[2].norm_x;
-    b.ln_launch[2 * l + 1] = l + 1 < L && !ln_in_epilogue[1] && !mrn::qkv_normalises(c, l + 1, M, bufs, norm);
   }
   GemmArgs v;
   v.m = b.positions, v.n = d, v.k = d, v.fp8 = false, v.status = c->status;
@@ -449,8 +363,7 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
   mrn::EmbedParams e{c->boards, c->piece, c->square, c->state, c->cast_w, c->cast_b, c->ep, c->x, c->t, c->square_start};
   const DevLayer& D0 = c->dl[0];
   mark(MRN_PROFILE_EMBED);
-  CK(mrn::launch_embed_ln(
-      e, mrn::NormParams{D0.n1g, D0.n1b, c->eps, b.embed_norm ? c->h : nullptr, act, 1.f / D0.as[0]}, P, d, s));
+  CK(mrn::launch_embed_ln(e, mrn::NormParams{D0.n1g, D0.n1b, c->eps, c->h, act, 1.f / D0.as[0]}, P, d, s));
   done();
   // Every later kernel follows a kernel of this pass, so its launch may overlap the end of that
   // one (the embedding follows the input copies and launches plainly). Not while profiling:
@@ -470,20 +383,14 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
     mark(MRN_PROFILE_GEMM);
     CK(mrn::gemm_launch(plans[1], s));
     done();
-    if (b.ln_launch[2 * l]) {
-      mark(MRN_PROFILE_LAYERNORM);
-      CK(mrn::launch_site_layernorm(c, l, 0, bufs, R, s));
-      done();
-    }
-    mark(MRN_PROFILE_GEMM);
-    if (b.mlp.empty()) {
-      CK(mrn::gemm_launch(plans[2], s));
-      CK(mrn::gemm_launch(plans[3], s));
-    } else {
-      CK(mrn::mlp_launch(b.mlp[l], s));
-    }
+    mark(MRN_PROFILE_LAYERNORM);
+    CK(mrn::launch_site_layernorm(c, l, 0, bufs, R, s));
     done();
-    if (b.ln_launch[2 * l + 1]) {
+    mark(MRN_PROFILE_GEMM);
+    CK(mrn::gemm_launch(plans[2], s));
+    CK(mrn::gemm_launch(plans[3], s));
+    done();
+    if (l + 1 < c->layers) {
       mark(MRN_PROFILE_LAYERNORM);
       CK(mrn::launch_site_layernorm(c, l, 1, bufs, R, s));
       done();
@@ -505,16 +412,9 @@ int enqueue(mrn_ctx* c, Bucket& b, cudaStream_t s, float* logits_out, Profiler* 
   return MRN_OK;
 }
 
-// Per layer: QKV, attention, out-proj, then FFN1 + FFN2 or the fused MLP.
-int layer_launches(const Bucket& b) { return b.mlp.empty() ? 5 : 4; }
-
-// Embedding, the layers' launches, a LayerNorm launch wherever no GEMM computes that norm (norm2,
-// and norm1 of every layer but the first), 3 for the heads.
-int launches_per_forward(const mrn_ctx* c, const Bucket& b) {
-  int n = 1 + layer_launches(b) * c->layers + 3;
-  for (uint8_t launch : b.ln_launch) n += launch;
-  return n;
-}
+// Embedding; per layer QKV, attention, out-proj, norm2, FFN1, FFN2; norm1 of every layer but the
+// first; 3 for the heads.
+int launches_per_forward(const mrn_ctx* c) { return 1 + 6 * c->layers + (c->layers - 1) + 3; }
 
 int get_bucket(mrn_ctx* c, int n, Bucket** out) {
   const int key = bucket_for(n);
@@ -606,6 +506,7 @@ void destroy(mrn_ctx* c) {
   if (c->h_wdl) cudaFreeHost(c->h_wdl);
   if (c->h_status) cudaFreeHost(c->h_status);
   if (c->stream) cudaStreamDestroy(c->stream);
+  if (c->pass_done) cudaEventDestroy(c->pass_done);
   delete c;
 }
 
@@ -679,8 +580,12 @@ MRN_API int mrn_create(const mrn_arch* arch, const mrn_weights* weights, int dev
   c->num_sms = prop.multiProcessorCount;
   if (mrn::gemm_prepare_device() != cudaSuccess || mrn::prepare_attention() != cudaSuccess)
     return bail(c->fail(MRN_ERR_CUDA, "kernel shared-memory attributes"));
+  if (mrn::load_row_kernels(c->d) != cudaSuccess) return bail(c->fail(MRN_ERR_CUDA, "loading the row kernels failed"));
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(c->fail(MRN_ERR_CUDA, "cudaStreamCreate failed"));
+  if (cudaEventCreateWithFlags(&c->pass_done, cudaEventDisableTiming) != cudaSuccess)
+    return bail(c->fail(MRN_ERR_CUDA, "cudaEventCreate failed"));
+  mrn::static_scratch_setup(c);
 
   if ((rc = load_weights(c, weights))) return bail(rc);
   if (precision == MRN_PRECISION_FP8)
@@ -725,6 +630,7 @@ int evaluate_host(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal
     src_b = c->h_boards, src_l = c->h_legal;
   }
   cudaStream_t s = c->stream;
+  if ((rc = mrn::begin_pass(c, s))) return rc;
   CK(cudaMemcpyAsync(c->boards, src_b, static_cast<size_t>(n) * MRN_BOARD_BYTES, cudaMemcpyHostToDevice, s));
   CK(cudaMemcpyAsync(c->legal, src_l, static_cast<size_t>(n) * MRN_MAX_LEGAL * 4, cudaMemcpyHostToDevice, s));
   if (P > n) {
@@ -739,6 +645,7 @@ int evaluate_host(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal
   CK(cudaMemcpyAsync(dst_p, src_p, prior_bytes, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(dst_w, c->wdl, static_cast<size_t>(n) * 3 * 4, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(c->h_status, c->status, 4, cudaMemcpyDeviceToHost, s));
+  if ((rc = mrn::end_pass(c, s))) return rc;
   // The inputs are checked while the GPU runs: the kernels clamp out-of-range tokens and flag
   // out-of-range actions themselves, so a bad batch costs one wasted pass, never a fault; its
   // outputs are discarded and the error names the first bad entry.
@@ -792,6 +699,7 @@ MRN_API int mrn_logits(mrn_ctx* c, int n, const uint8_t* boards, float* policy, 
   const int P = b->positions;
   if (!c->logits && (rc = dev_alloc(c, &c->logits, static_cast<size_t>(c->max_bucket) * MRN_ACTIONS * 4))) return rc;
   cudaStream_t s = c->stream;
+  if ((rc = mrn::begin_pass(c, s))) return rc;
   CK(cudaMemcpyAsync(c->boards, boards, static_cast<size_t>(n) * MRN_BOARD_BYTES, cudaMemcpyHostToDevice, s));
   if (P > n)
     CK(cudaMemsetAsync(c->boards + static_cast<size_t>(n) * MRN_BOARD_BYTES, 0, static_cast<size_t>(P - n) * MRN_BOARD_BYTES, s));
@@ -799,6 +707,7 @@ MRN_API int mrn_logits(mrn_ctx* c, int n, const uint8_t* boards, float* policy, 
   CK(cudaMemcpyAsync(policy, c->logits, static_cast<size_t>(n) * MRN_ACTIONS * 4, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(value, c->wdl, static_cast<size_t>(n) * 3 * 4, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(c->h_status, c->status, 4, cudaMemcpyDeviceToHost, s));
+  if ((rc = mrn::end_pass(c, s))) return rc;
   CK(cudaStreamSynchronize(s));
   const int word = *c->h_status;
   if (word) {
@@ -823,6 +732,7 @@ MRN_API int mrn_evaluate_device(mrn_ctx* c, int n, const uint8_t* d_boards, cons
   if (rc) return rc;
   const int P = b->positions;
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  if ((rc = mrn::begin_pass(c, s))) return rc;
   CK(cudaMemcpyAsync(c->boards, d_boards, static_cast<size_t>(n) * MRN_BOARD_BYTES, cudaMemcpyDeviceToDevice, s));
   CK(cudaMemcpyAsync(c->legal, d_legal, static_cast<size_t>(n) * MRN_MAX_LEGAL * 4, cudaMemcpyDeviceToDevice, s));
   if (P > n) {
@@ -832,7 +742,7 @@ MRN_API int mrn_evaluate_device(mrn_ctx* c, int n, const uint8_t* d_boards, cons
   CK(cudaGraphLaunch(b->graph, s));
   CK(cudaMemcpyAsync(d_priors, c->priors, static_cast<size_t>(n) * MRN_MAX_LEGAL * 4, cudaMemcpyDeviceToDevice, s));
   CK(cudaMemcpyAsync(d_wdl, c->wdl, static_cast<size_t>(n) * 3 * 4, cudaMemcpyDeviceToDevice, s));
-  return MRN_OK;
+  return mrn::end_pass(c, s);
 }
 
 MRN_API int mrn_status_word(mrn_ctx* c, int* word) {
@@ -857,6 +767,7 @@ MRN_API int mrn_profile(mrn_ctx* c, int n, const uint8_t* d_boards, const int32_
   if (rc) return rc;
   const int P = b->positions;
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  if ((rc = mrn::begin_pass(c, s))) return rc;
   CK(cudaMemcpyAsync(c->boards, d_boards, static_cast<size_t>(n) * MRN_BOARD_BYTES, cudaMemcpyDeviceToDevice, s));
   CK(cudaMemcpyAsync(c->legal, d_legal, static_cast<size_t>(n) * MRN_MAX_LEGAL * 4, cudaMemcpyDeviceToDevice, s));
   if (P > n) {
@@ -877,14 +788,15 @@ MRN_API int mrn_profile(mrn_ctx* c, int n, const uint8_t* d_boards, const int32_
   }
   if (rc) return rc;
   for (size_t i = 0; i < b->plans.size(); ++i) flops[MRN_PROFILE_GEMM] += mrn::gemm_flops(b->plans[i].args);
-  launches[MRN_PROFILE_GEMM] = static_cast<int>(b->plans.size()) - (b->mlp.empty() ? 0 : c->layers);
+  launches[MRN_PROFILE_GEMM] = static_cast<int>(b->plans.size());
   launches[MRN_PROFILE_EMBED] = 1;
   launches[MRN_PROFILE_ATTENTION] = c->layers;
-  launches[MRN_PROFILE_LAYERNORM] = launches_per_forward(c, *b) - (1 + layer_launches(*b) * c->layers + 3);
+  launches[MRN_PROFILE_LAYERNORM] = 2 * c->layers - 1;
   launches[MRN_PROFILE_HEADS] = 2;
   flops[MRN_PROFILE_ATTENTION] = 4.0 * P * static_cast<double>(c->t) * c->t * c->d * c->layers;
   CK(cudaMemcpyAsync(d_priors, c->priors, static_cast<size_t>(n) * MRN_MAX_LEGAL * 4, cudaMemcpyDeviceToDevice, s));
   CK(cudaMemcpyAsync(d_wdl, c->wdl, static_cast<size_t>(n) * 3 * 4, cudaMemcpyDeviceToDevice, s));
+  if ((rc = mrn::end_pass(c, s))) return rc;
   CK(cudaStreamSynchronize(s));
   return MRN_OK;
 }
@@ -895,7 +807,7 @@ MRN_API int mrn_launches_per_forward(mrn_ctx* c, int n) {
   if (n < 1 || n > c->max_batch) return -1;
   Bucket* b = nullptr;
   if (cudaSetDevice(c->device) != cudaSuccess || get_bucket(c, n, &b)) return -1;
-  return launches_per_forward(c, *b);
+  return launches_per_forward(c);
 }
 
 MRN_API const char* mrn_describe(mrn_ctx* c) { return c ? c->describe.c_str() : ""; }

@@ -31,13 +31,7 @@ struct DevLayer {
 
 struct Bucket {
   int positions = 0;
-  std::vector<GemmPlan> plans;  // 4 per layer, then the value head's first layer
-  // Per layer: [2l] a LayerNorm launch (norm2) follows out-proj, [2l+1] one (the next layer's
-  // norm1) follows FFN2. 0 where the norm runs inside a GEMM: in the consuming GEMM's A operand
-  // (gemm_norm.cuh) or in the residual GEMM's epilogue (gemm_ln.cuh).
-  std::vector<uint8_t> ln_launch;
-  bool embed_norm = true;  // the embedding kernel writes layer 0's norm1 (its QKV does not normalise A)
-  std::vector<MlpPlan> mlp;  // per layer when FFN1 + FFN2 run as one fused MLP launch (else empty)
+  std::vector<GemmPlan> plans;  // 4 per layer (QKV, out-proj, FFN1, FFN2), then the value head's first layer
   cudaGraphExec_t graph = nullptr;
 };
 
@@ -115,6 +109,17 @@ struct mrn_ctx {
   float* h_wdl = nullptr;
   int* h_status = nullptr;
 
+  // Ordering of the passes on this context's buffers across streams: every entry point that
+  // enqueues a pass makes its stream wait for `pass_done` when the previous pass ran on another
+  // stream (`pass_stream`), and records `pass_done` on its own stream after the pass.
+  cudaEvent_t pass_done = nullptr;
+  cudaStream_t pass_stream = nullptr;
+  bool pass_recorded = false;
+  // Device address of static_forward.cu's scratch array on this context's device, looked up in
+  // mrn_create with the device current (nullptr, with the reason in static_error, if that failed).
+  uint8_t* static_scratch = nullptr;
+  std::string static_error;
+
   std::map<int, mrn::Bucket> buckets;
   std::string describe;
   std::string last_error;
@@ -131,32 +136,22 @@ struct mrn_ctx {
 };
 
 namespace mrn {
-// The four GEMMs of layer `l` over `rows` rows: QKV, out-proj, FFN1, FFN2. With `norm`, QKV and
-// FFN1 compute norm1 / norm2 of x themselves where the normalised-A kernel supports the shape.
-// With `fuse`, out-proj carries norm2 and FFN2 (all layers but the last) the next layer's norm1 as
-// the fused residual + LayerNorm epilogue, unless the consuming GEMM normalises A itself.
-// With `mlp`, FFN1 and FFN2 are planned for the fused MLP kernel (mlp_args): FFN1 reads h and FFN2
-// carries no LayerNorm.
-void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool fuse, bool norm, bool mlp,
-                     GemmArgs (&g)[4]);
-// The fused MLP of a layer from its FFN1 and FFN2 arguments; false where the kernel does not
-// support the layer (not e4m3, d != 512, ...).
-bool mlp_args(const GemmArgs& ffn1, const GemmArgs& ffn2, MlpArgs* out);
-// Whether FFN1 + FFN2 run as one fused launch (environment MRN_MLP=1; off by default).
-bool mlp_enabled();
+// Before a pass on stream `s`: wait for the context's previous pass if it was enqueued on another
+// stream (no-op while `s` is being captured into a graph: ordering captured work is the
+// capturer's). After the pass: record its completion on `s`. Both return an mrn_status.
+int begin_pass(mrn_ctx* c, cudaStream_t s);
+int end_pass(mrn_ctx* c, cudaStream_t s);
+// Looks up the static scratch array's device address for c (static_forward.cu); called by
+// mrn_create with c's device current.
+void static_scratch_setup(mrn_ctx* c);
+// The four GEMMs of layer `l` over `rows` rows: QKV, out-proj, FFN1, FFN2.
+void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, GemmArgs (&g)[4]);
 // Whether the kernels after the first of a pass over `positions` positions launch with
 // programmatic dependent launch (environment MRN_PDL: 1 always, 0 never; by default for small
 // batches).
 bool pdl_enabled(int positions);
-// Whether layer l's QKV GEMM computes norm1 itself (under the same `norm` setting).
-bool qkv_normalises(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, bool norm);
-// Whether plans use the fused residual + LayerNorm epilogue (environment MRN_GEMM_LN=1; off by default).
-bool ln_fusion_enabled();
-// Whether QKV and FFN1 normalise their A operand in the kernel (environment MRN_GEMM_NORM=1; off by
-// default: the CTA-pair kernel it needs is slower at K = d than LayerNorm launch + single-CTA GEMM).
-bool norm_a_enabled();
-// The LayerNorm launch that stands in for an unfused site: norm2 of layer `l` (site 0) or norm1 of
-// layer l + 1 (site 1), from x into h.
+// The LayerNorm after a residual GEMM: norm2 of layer `l` (site 0) or norm1 of layer l + 1
+// (site 1), from x into h.
 cudaError_t launch_site_layernorm(const mrn_ctx* c, int l, int site, const LayerBuffers& b, int rows,
                                   cudaStream_t s);
 }  // namespace mrn

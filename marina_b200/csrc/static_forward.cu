@@ -8,16 +8,18 @@
 // They can still evaluate small batches (the search's root, a handful of leaves) through
 // `mrn_evaluate_device_static`, with the weights already loaded by `mrn_create`.
 //
-// The array holds kStaticScratchBytes (8 MiB) and is resident on every GPU that loads this
-// library, for the life of the process. How many positions fit depends on the network: one
+// The array holds kStaticScratchBytes (8 MiB) and is resident on every GPU on which a context has
+// been created, for the life of the process. How many positions fit depends on the network: one
 // position needs 65 rows of the residual stream (f16), the two GEMM inputs and the attention
 // output (bf16, or e4m3 for MRN_PRECISION_FP8), Q/K/V (bf16) and the FFN hidden layer, plus
 // two d-wide bf16 rows for the value head -- 0.67 MB for the `small` network in bf16 or fp8w
 // (12 positions; 17 in fp8) and 0.25 MB for `nano` (33 positions; 47 in fp8). Larger batches
 // are refused with MRN_ERR_BATCH_TOO_LARGE and a message naming the limit.
 //
-// The first call on a device looks up the array's device address (cudaGetSymbolAddress, once
-// per device, with that device current); make that first call before capturing a stream.
+// mrn_create looks the array's device address up (cudaGetSymbolAddress, with the context's device
+// current) and keeps it in the context. That first look-up loads the module holding the array, which
+// is when the device memory for it is allocated, so by the time a caller needs the no-allocation
+// guarantee the array is already resident; mrn_create also loads every kernel the pass launches.
 //
 // All calls on a device share the array. Nothing in it has to start at zero (every buffer is
 // written before it is read), so nothing is cleared, but two calls whose GPU work overlaps --
@@ -27,7 +29,7 @@
 #include <cuda_bf16.h>
 #include <stdio.h>
 
-#include <mutex>
+#include <string>
 
 #include "../../include/marina_b200.h"
 #include "gemm.h"
@@ -38,12 +40,8 @@
 namespace {
 
 constexpr size_t kStaticScratchBytes = size_t(8) << 20;
-constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
-
-std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
 
 size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
 
@@ -72,22 +70,6 @@ int max_positions(const mrn_ctx* c) {
   return n;
 }
 
-// The device address of the array on the current device, looked up once per device: in host
-// code `g_static_scratch` names a host-side stand-in, not device memory.
-int scratch_address(mrn_ctx* c, uint8_t** out) {
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (c->device < 0 || c->device >= kMaxDevices) return c->fail(MRN_ERR_UNSUPPORTED, "device %d", c->device);
-  if (!g_scratch_addr[c->device]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
-    if (e != cudaSuccess || !p)
-      return c->fail(MRN_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
-    g_scratch_addr[c->device] = p;
-  }
-  *out = static_cast<uint8_t*>(g_scratch_addr[c->device]);
-  return MRN_OK;
-}
-
 #define CKS(call)                                                                                    \
   do {                                                                                               \
     const cudaError_t e_ = (call);                                                                   \
@@ -100,26 +82,6 @@ int gemm(mrn_ctx* c, const mrn::GemmArgs& a, cudaStream_t s) {
   char err[256];
   if (!mrn::gemm_plan(&p, a, c->num_sms, err)) return c->fail(MRN_ERR_UNSUPPORTED, "%s", err);
   CKS(mrn::gemm_launch(p, s));
-  return MRN_OK;
-}
-
-// A residual GEMM and the LayerNorm after it (norm2 of layer l at site 0, norm1 of layer l + 1 at
-// site 1): in the epilogue where that plans, else the plain residual GEMM followed by a LayerNorm
-// launch when the next GEMM reads h (`need_h`: not after the last layer, nor where the next GEMM
-// normalises x itself).
-int residual(mrn_ctx* c, int l, int site, mrn::GemmArgs a, const mrn::LayerBuffers& b, bool need_h, cudaStream_t s) {
-  mrn::GemmPlan p;
-  char err[256];
-  if (a.epi == mrn::Epilogue::kResidualLn) {
-    if (mrn::gemm_plan(&p, a, c->num_sms, err)) {
-      CKS(mrn::gemm_launch(p, s));
-      return MRN_OK;
-    }
-    a.epi = mrn::Epilogue::kResidual;
-  }
-  if (!mrn::gemm_plan(&p, a, c->num_sms, err)) return c->fail(MRN_ERR_UNSUPPORTED, "%s", err);
-  CKS(mrn::gemm_launch(p, s));
-  if (need_h) CKS(mrn::launch_site_layernorm(c, l, site, b, a.m, s));
   return MRN_OK;
 }
 
@@ -141,42 +103,23 @@ int forward(mrn_ctx* c, int n, const uint8_t* boards, const int32_t* legal, floa
 
   const mrn::DevLayer& D0 = c->dl[0];
   const mrn::LayerBuffers bufs{h, qkv, attn, ff, x};
-  const bool fuse = mrn::ln_fusion_enabled(), norm = mrn::norm_a_enabled();
-  bool mlp = mrn::mlp_enabled();
-  for (int l = 0; l < c->layers && mlp; ++l) {
-    mrn::GemmArgs g[4];
-    mrn::MlpArgs a;
-    mrn::layer_gemm_args(c, l, R, bufs, fuse, norm, true, g);
-    mlp = mrn::mlp_args(g[2], g[3], &a);
-  }
   CKS(mrn::launch_embed_ln(
       mrn::EmbedParams{boards, c->piece, c->square, c->state, c->cast_w, c->cast_b, c->ep, x, c->t, c->square_start},
-      mrn::NormParams{D0.n1g, D0.n1b, c->eps, mrn::qkv_normalises(c, 0, R, bufs, norm) ? nullptr : h, act,
-                      1.f / D0.as[0]},
-      n, d, s));
+      mrn::NormParams{D0.n1g, D0.n1b, c->eps, h, act, 1.f / D0.as[0]}, n, d, s));
   // The kernels after the embedding follow one of this pass: their launches may overlap.
   const mrn::PdlScope pdl(mrn::pdl_enabled(n));
   for (int l = 0; l < c->layers; ++l) {
     const mrn::DevLayer& D = c->dl[l];
     mrn::GemmArgs g[4];
-    mrn::layer_gemm_args(c, l, R, bufs, fuse, norm, mlp, g);
+    mrn::layer_gemm_args(c, l, R, bufs, g);
     if ((rc = gemm(c, g[0], s))) return rc;
     CKS(mrn::launch_attention(mrn::AttentionParams{qkv, attn, act, 1.f / D.as[1], c->t, d, c->heads, c->status}, n,
                               d / c->heads, s));
-    if ((rc = residual(c, l, 0, g[1], bufs, !g[2].norm_x, s))) return rc;
-    const bool need_h = l + 1 < c->layers && !mrn::qkv_normalises(c, l + 1, R, bufs, norm);
-    if (mlp) {
-      mrn::MlpArgs a;
-      mrn::MlpPlan mp;
-      char err[256];
-      mrn::mlp_args(g[2], g[3], &a);
-      if (!mrn::mlp_plan(&mp, a, c->num_sms, err)) return c->fail(MRN_ERR_UNSUPPORTED, "%s", err);
-      CKS(mrn::mlp_launch(mp, s));
-      if (need_h) CKS(mrn::launch_site_layernorm(c, l, 1, bufs, R, s));
-    } else {
-      if ((rc = gemm(c, g[2], s))) return rc;
-      if ((rc = residual(c, l, 1, g[3], bufs, need_h, s))) return rc;
-    }
+    if ((rc = gemm(c, g[1], s))) return rc;
+    CKS(mrn::launch_site_layernorm(c, l, 0, bufs, R, s));
+    if ((rc = gemm(c, g[2], s))) return rc;
+    if ((rc = gemm(c, g[3], s))) return rc;
+    if (l + 1 < c->layers) CKS(mrn::launch_site_layernorm(c, l, 1, bufs, R, s));
   }
   mrn::HeadsParams hp;
   hp.x = x, hp.final_g = c->fn_g, hp.final_b = c->fn_b, hp.policy_g = c->pn_g, hp.policy_b = c->pn_b;
@@ -206,11 +149,29 @@ extern "C" MRN_API int mrn_evaluate_device_static(mrn_ctx* c, int n, const uint8
     return c->fail(MRN_ERR_BATCH_TOO_LARGE,
                    "batch of %d positions exceeds the %d that fit the %zu-byte static scratch for this network", n,
                    limit, kStaticScratchBytes);
+  if (!c->static_scratch)
+    return c->fail(MRN_ERR_CUDA, "the static scratch array is not available on device %d: %s", c->device,
+                   c->static_error.c_str());
   const cudaError_t e = cudaSetDevice(c->device);
   if (e != cudaSuccess) return c->fail(MRN_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
-  uint8_t* base = nullptr;
-  const int rc = scratch_address(c, &base);
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  int rc = mrn::begin_pass(c, s);
   if (rc) return rc;
-  return forward(c, n, d_boards, d_legal, d_priors, d_wdl, base,
-                 stream ? static_cast<cudaStream_t>(stream) : c->stream);
+  if ((rc = forward(c, n, d_boards, d_legal, d_priors, d_wdl, c->static_scratch, s))) return rc;
+  return mrn::end_pass(c, s);
 }
+
+namespace mrn {
+
+void static_scratch_setup(mrn_ctx* c) {
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+  if (e != cudaSuccess || !p) {
+    cudaGetLastError();
+    c->static_error = std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e);
+    return;
+  }
+  c->static_scratch = static_cast<uint8_t*>(p);
+}
+
+}  // namespace mrn

@@ -3,10 +3,11 @@
 ``B200Network`` is the drop-in for ``CudaNetwork`` (src/net/cuda/mod.rs:225-1012): it
 owns one library context (``mrn_ctx``) on one GPU, packs leaves the way the reference's CUDA
 backend does (src/net/cuda/mod.rs:946-967) and slices each position's priors out of the
-224-slot output (:994-999). ``ShardedNetwork`` implements the same trait over several
-GPUs: every batch is split into contiguous shards, one per GPU, evaluated concurrently by
-one evaluator thread per GPU, and concatenated in order (no collective: the positions are
-independent). Errors surface as ``NetworkError``; nothing is ever substituted for a
+224-slot output (:994-999). ``GroupNetwork`` implements the same trait over several GPUs
+through the library's own multi-device evaluator (``mrn_group_*``: contiguous shards, one
+per GPU, evaluated at the same time by native per-device threads and written back in
+order); ``ShardedNetwork`` does the same from Python threads over any replicas. No
+collective is involved: the positions are independent. Errors surface as ``NetworkError``; nothing is ever substituted for a
 network's answer (src/net/mod.rs:284-288).
 """
 
@@ -249,6 +250,68 @@ class B200Network(Network):
         if getattr(self, "_ctx", None):
             self._lib.mrn_destroy(self._ctx)
             self._ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class GroupNetwork(Network):
+    """`Network` over one weight replica per listed device through `mrn_group_create` /
+    `mrn_group_evaluate`: every batch is cut into contiguous shards (sizes differing by at most
+    one position), evaluated at the same time by the library's per-device threads and written
+    into the outputs in input order. A failing shard raises `NetworkError` naming its device."""
+
+    def __init__(self, arch: Architecture, weights: Weights, devices: Sequence[int], max_batch: int = 1024,
+                 precision: str = "fp8w"):
+        self._lib = _lib.load()
+        if precision not in _lib.PRECISIONS:
+            raise ValueError(f"precision {precision!r}: one of {sorted(_lib.PRECISIONS)}")
+        self.arch, self.devices, self.max_batch, self.precision = arch, list(devices), max_batch, precision
+        ca, amax = c_arch(arch)
+        cw, layers = c_weights(weights)
+        devs = (c_int * len(self.devices))(*self.devices)
+        group = c_void_p()
+        rc = self._lib.mrn_group_create(ctypes.byref(ca), ctypes.byref(cw), devs, len(self.devices), max_batch,
+                                        _lib.PRECISIONS[precision], ctypes.byref(group))
+        del amax, layers
+        if rc != 0:
+            raise NetworkError(f"b200 group failed to load: {self._lib.mrn_group_last_error(None).decode()}", rc)
+        self._group = group
+
+    def evaluate(self, batch: Sequence[Leaf]) -> list[Evaluation]:
+        boards, legal, counts = pack(batch)
+        priors, wdl = self.evaluate_packed(boards, legal)
+        return unpack(priors, wdl, counts)
+
+    def evaluate_packed(self, boards: np.ndarray, legal: np.ndarray, priors: np.ndarray | None = None,
+                        wdl: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:
+        """`mrn_group_evaluate` on packed host arrays (see `B200Network.evaluate_packed`)."""
+        boards = np.ascontiguousarray(boards, dtype=np.uint8)
+        legal = np.ascontiguousarray(legal, dtype=np.int32)
+        n = boards.shape[0]
+        if boards.shape != (n, BOARD_BYTES) or legal.shape != (n, MAX_LEGAL):
+            raise ValueError("boards must be [n, 66] and legal [n, 224]")
+        if priors is None:
+            priors = np.empty((n, MAX_LEGAL), dtype=np.float32)
+        if wdl is None:
+            wdl = np.empty((n, 3), dtype=np.float32)
+        rc = self._lib.mrn_group_evaluate(self._group, n, boards.ctypes.data_as(POINTER(c_uint8)),
+                                          legal.ctypes.data_as(POINTER(c_int32)), _f32p(priors), _f32p(wdl))
+        if rc != 0:
+            raise NetworkError(f"b200 group forward failed: {self._lib.mrn_group_last_error(self._group).decode()}",
+                               rc)
+        return priors, wdl
+
+    def describe(self) -> str:
+        return self._lib.mrn_group_describe(self._group).decode()
+
+    def close(self) -> None:
+        if getattr(self, "_group", None):
+            self._lib.mrn_group_destroy(self._group)
+            self._group = None
 
     def __del__(self):
         try:

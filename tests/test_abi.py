@@ -28,6 +28,47 @@ def test_evaluator_exports_every_declared_symbol():
     assert set(_lib.EXPORTS) >= set(names)
 
 
+def test_evaluator_exports_nothing_but_the_header():
+    """The drop-in library exports exactly the evaluator ABI: no test hooks."""
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.split()[1:2] == ["T"]}
+    mrn = {name for name in exported if name.startswith("mrn_")}
+    assert mrn == set(_declared("marina_b200.h", "MRN_API")), mrn ^ set(_declared("marina_b200.h", "MRN_API"))
+    assert not any(name.startswith("mrn_test") for name in exported)
+
+
+def test_test_library_exports_every_declared_symbol():
+    names = _declared("marina_b200_test.h", "MRN_TEST_API")
+    assert "mrn_test_gemm_wait_expiry" in names
+    lib = _lib.load_test()
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(_lib.TEST_EXPORTS) == set(names)
+
+
+def test_group_entry_points_refuse_bad_arguments():
+    """mrn_group_create checks its device list before touching a device; mrn_group_evaluate
+    refuses a NULL group; both messages come back through mrn_group_last_error(NULL)."""
+    lib = _lib.load()
+    arch = model.Architecture(64, 1, 2, 128)
+    from marina_b200.network import c_arch, c_weights
+
+    ca, amax = c_arch(arch)
+    cw, layers = c_weights(weights.random_init(arch))
+    out = ctypes.c_void_p()
+    assert lib.mrn_group_create(ctypes.byref(ca), ctypes.byref(cw), None, 0, 8, 0, ctypes.byref(out)) == 1
+    assert b"at least one device" in lib.mrn_group_last_error(None)
+    devs = (ctypes.c_int * 1)(0)
+    assert lib.mrn_group_create(ctypes.byref(ca), ctypes.byref(cw), devs, 1, 0, 0, ctypes.byref(out)) == 1
+    assert b"max_batch" in lib.mrn_group_last_error(None)
+    assert lib.mrn_group_evaluate(None, 1, None, None, None, None) == 1
+    assert b"group is NULL" in lib.mrn_group_last_error(None)
+    assert lib.mrn_group_size(None) == 0 and lib.mrn_group_context(None, 0) is None
+
+
 def test_chess_library_exports_every_declared_symbol():
     names = _declared("marina_chess.h", "MRC_API")
     lib = chess.load()

@@ -1,6 +1,5 @@
-"""The attention kernels against a plain PyTorch fp32 softmax attention on the same bf16 Q, K, V:
-the default mma.sync kernel (per position and head, 65 tokens), and for head_dim 64 the opt-in
-tcgen05 kernel (MRN_ATTN_TC=1, run in a child process: the switch is read once per process)."""
+"""The attention kernel against a plain PyTorch fp32 softmax attention on the same bf16 Q, K, V
+(per position and head, 65 tokens; head_dim 64 and 32), through the test library."""
 
 import ctypes
 
@@ -16,7 +15,7 @@ T = 65
 
 
 def _attention(qkv, positions, d, heads, e4m3, inv_q):
-    lib = _lib.load()
+    lib = _lib.load_test()
     out = torch.full((positions * T + 16, d), 0x55 if e4m3 else 7.0, device=qkv.device,
                      dtype=torch.uint8 if e4m3 else torch.bfloat16)
     status = torch.zeros(1, dtype=torch.int32, device=qkv.device)
@@ -72,28 +71,3 @@ def test_attention_matches_torch(cuda, d, heads, positions, e4m3):
         where = [(r % T, c // (d // heads), c % (d // heads), float(got[r, c]), float(ref[r, c])) for r, c in idx]
         raise AssertionError(f"{int(bad.sum())} out of tolerance, max err {float(err.max())}; "
                              f"(token, head, col, got, ref): {where}")
-
-
-TC_SCRIPT = r"""
-import sys
-sys.path.insert(0, sys.argv[1])
-import torch
-from tests import test_attention_gpu as t
-for positions in (1, 3, 37, 300):
-    for e4m3 in (False, True):
-        t.test_attention_matches_torch(torch.device("cuda", 0), 512, 8, positions, e4m3)
-print("ok")
-"""
-
-
-def test_tcgen05_attention_matches_torch(cuda):
-    """The same checks on the tcgen05 kernel (S and O in TMEM, P written back to TMEM as the second
-    MMA's A operand, V as an N-major B operand)."""
-    import os
-    import subprocess
-    import sys
-
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    r = subprocess.run([sys.executable, "-c", TC_SCRIPT, root], env=dict(os.environ, MRN_ATTN_TC="1"), cwd=root,
-                       capture_output=True, text=True, timeout=600)
-    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-2000:]

@@ -351,80 +351,35 @@ def _check_plans_against_oracle(outs, net, precision):
         check(compare(out["priors"], out["wdl"], ref_p, ref_w, counts), precision)
 
 
-@pytest.mark.parametrize("net,precision", [("small", "bf16"), ("small", "fp8"), ("nano", "fp8w")])
-def test_fused_and_unfused_layernorm_plans(tmp_path, net, precision):
-    """The residual GEMMs with the following LayerNorm fused in (MRN_GEMM_LN=1, no LayerNorm
-    launches) and the plain residual GEMM + LayerNorm launches (MRN_GEMM_LN=0) agree, and both
-    meet the oracle bounds (QKV and FFN1 read h, MRN_GEMM_NORM=0)."""
-    outs = _run_plans(tmp_path, net, precision, {"0": {"MRN_GEMM_LN": "0", "MRN_GEMM_NORM": "0"},
-                                                 "1": {"MRN_GEMM_LN": "1", "MRN_GEMM_NORM": "0"}})
+@pytest.mark.parametrize("net,precision", [("small", "fp8w"), ("small", "bf16"), ("small", "fp8")])
+def test_cta_pair_plans(tmp_path, net, precision):
+    """The GEMMs planned on CTA pairs from K = 512 (MRN_GEMM_PAIR=2: QKV and FFN1 as well), only from
+    K = 1024 (the default below, FFN2) and never (MRN_GEMM_PAIR=0) agree with each other to f32
+    accumulation order and each meets the oracle bounds."""
+    outs = _run_plans(tmp_path, net, precision, {"never": {"MRN_GEMM_PAIR": "0"}, "k1024": {"MRN_GEMM_PAIR": "1"},
+                                                 "k512": {"MRN_GEMM_PAIR": "2"}})
     layers = card(net).n_layers
-    assert int(outs["0"]["launches"]) == 7 * layers + 3 and int(outs["1"]["launches"]) == 5 * layers + 4
-    counts = outs["1"]["counts"]
-    # same arithmetic up to rounding order (one f16 rounding per residual add instead of two)
-    m = compare(outs["1"]["priors"], outs["1"]["wdl"], outs["0"]["priors"], outs["0"]["wdl"], counts)
-    print(m)
-    tight = precision != "fp8"
-    assert m["wdl"] <= (2e-3 if tight else WDL_TOL) and m["prior"] <= (2e-3 if tight else PRIOR_TOL), m
-    _check_plans_against_oracle(outs, net, precision)
-
-
-@pytest.mark.parametrize("net,precision", [("small", "fp8"), ("small", "bf16"), ("nano", "fp8")])
-def test_normalised_a_plans(tmp_path, net, precision):
-    """QKV and FFN1 normalising x in the GEMM (MRN_GEMM_NORM=1, where the kernel supports the
-    shape: `small` with e4m3 operands) against LayerNorm launches into h (the default). The GEMMs see
-    the same e4m3 A either way (the GEMMs differ only in tile shape: 256-row CTA-pair tiles
-    against 128-row ones), so the outputs agree to accumulation order; elsewhere the switch
-    changes nothing."""
-    outs = _run_plans(tmp_path, net, precision, {"norm0": {"MRN_GEMM_NORM": "0", "MRN_GEMM_LN": "0"},
-                                                 "norm1": {"MRN_GEMM_NORM": "1", "MRN_GEMM_LN": "0"}})
-    layers = card(net).n_layers
-    normalised = net == "small" and precision == "fp8"
-    assert int(outs["norm0"]["launches"]) == 7 * layers + 3
-    assert int(outs["norm1"]["launches"]) == (5 * layers + 4 if normalised else 7 * layers + 3)
-    counts = outs["norm1"]["counts"]
-    m = compare(outs["norm1"]["priors"], outs["norm1"]["wdl"], outs["norm0"]["priors"], outs["norm0"]["wdl"], counts)
-    print(m)
-    if normalised:
-        assert m["wdl"] <= WDL_TOL and m["prior"] <= PRIOR_TOL, m
-    else:
-        assert m["wdl"] == 0 and m["prior"] == 0, m
-    _check_plans_against_oracle(outs, net, precision)
-
-
-@pytest.mark.parametrize("net,precision", [("small", "fp8"), ("small", "bf16"), ("nano", "fp8")])
-def test_fused_mlp_plans(tmp_path, net, precision):
-    """FFN1 + FFN2 as one fused MLP launch per layer (MRN_MLP=1, where the kernel supports the
-    layer: `small` with e4m3 operands) against the two GEMM launches (the default). The hidden
-    values and the FFN2 accumulation order are the same, so the outputs agree to rounding; elsewhere
-    the switch changes nothing."""
-    outs = _run_plans(tmp_path, net, precision, {"mlp0": {"MRN_MLP": "0", "MRN_GEMM_LN": "0"},
-                                                 "mlp1": {"MRN_MLP": "1", "MRN_GEMM_LN": "0"}})
-    layers = card(net).n_layers
-    fused = net == "small" and precision == "fp8"
-    assert int(outs["mlp0"]["launches"]) == 7 * layers + 3
-    assert int(outs["mlp1"]["launches"]) == (6 * layers + 3 if fused else 7 * layers + 3)
-    counts = outs["mlp1"]["counts"]
-    m = compare(outs["mlp1"]["priors"], outs["mlp1"]["wdl"], outs["mlp0"]["priors"], outs["mlp0"]["wdl"], counts)
-    print(m)
-    if fused:
-        assert m["wdl"] <= WDL_TOL and m["prior"] <= PRIOR_TOL, m
-    else:
-        assert m["wdl"] == 0 and m["prior"] == 0, m
+    counts = outs["never"]["counts"]
+    for key in ("k1024", "k512"):
+        assert int(outs[key]["launches"]) == 7 * layers + 3
+        m = compare(outs[key]["priors"], outs[key]["wdl"], outs["never"]["priors"], outs["never"]["wdl"], counts)
+        print(key, m)
+        tight = precision != "fp8"
+        assert m["wdl"] <= (2e-3 if tight else WDL_TOL) and m["prior"] <= (2e-3 if tight else PRIOR_TOL), m
     _check_plans_against_oracle(outs, net, precision)
 
 
 @pytest.mark.parametrize("net,precision,extra", [
     ("small", "fp8", {}),
     ("nano", "bf16", {}),
-    ("small", "fp8", {"MRN_GEMM_NORM": "1", "MRN_MLP": "1", "MRN_ATTN_TC": "1"}),
-    ("small", "bf16", {"MRN_GEMM_LN": "1"}),
+    ("small", "fp8w", {}),
+    ("small", "fp8w", {"MRN_GEMM_PAIR": "2"}),
 ])
 def test_programmatic_launch_changes_no_result(tmp_path, net, precision, extra):
     """Kernels launched with programmatic dependent launch (MRN_PDL=1: each kernel's launch and
     set-up overlap the end of the previous one, and it waits for that grid before touching memory)
     give the same bits as plain stream-ordered launches (MRN_PDL=0), for the default plans and for
-    the opt-in kernels."""
+    CTA-pair plans from K = 512."""
     outs = _run_plans(tmp_path, net, precision, {"plain": dict(extra, MRN_PDL="0"), "pdl": dict(extra, MRN_PDL="1")})
     assert int(outs["plain"]["launches"]) == int(outs["pdl"]["launches"])
     assert np.array_equal(outs["plain"]["priors"], outs["pdl"]["priors"])

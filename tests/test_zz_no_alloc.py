@@ -5,7 +5,8 @@ uses the context's own buffers, through the C ABI.
 
 The static entry point keeps every intermediate buffer in one 8 MiB array compiled into the
 library and shared by all calls on a device, so it is called twice in a row here to show that
-the second call does not depend on what the first left in the array. Both entry points run
+the second call does not depend on what the first left in the array, and that neither call
+changes the device's free memory. Both entry points run
 the same kernels on the same inputs, so they agree to 1e-6 (the tolerance this suite uses for
 GPU-to-GPU comparisons). This file sorts last so a failure here does not stop the rest of the
 suite; it also runs on its own in a fresh process."""
@@ -50,9 +51,14 @@ def test_static_scratch_forward_matches_the_allocating_entry_point(net, precisio
         out_p = torch.full((n, 224), float("nan"), device=dev)
         out_w = torch.full((n, 3), float("nan"), device=dev)
         torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info(dev)[0]
         ev.evaluate_device_static(n, db.data_ptr(), dl.data_ptr(), out_p.data_ptr(), out_w.data_ptr(),
                                   stream.cuda_stream)
         stream.synchronize()
+        free_after = torch.cuda.mem_get_info(dev)[0]
+        # The property the entry point exists for: no device memory is allocated by the call
+        # (the array and the kernels were loaded by mrn_create), the first call included.
+        assert free_after == free_before, (call, free_before - free_after)
         assert ev.status_word() == 0, call
         assert float((out_p - ref_p).abs().max()) <= 1e-6, call
         assert float((out_w - ref_w).abs().max()) <= 1e-6, call
