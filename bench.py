@@ -4,10 +4,13 @@ PUCT search calls on each leaf minibatch (src/net/mod.rs:290-296, src/search/mod
 One step = one forward pass of a batch of synthetic leaf positions (uniform-random legal
 playouts of 0-80 plies, encoded as the reference encodes them) through the `small` network
 (d_model 512, 12 layers, 8 heads, d_ff 2048, random init N(0, 0.02) seed 0, per-tensor e4m3
-weights) on every GPU. Each GPU holds a full weight replica and evaluates its own batch (weak
-scaling, no collective on the data path; NCCL only carries the barrier and the max over ranks).
+weights) on every GPU. The default precision is fp8w: the weights e4m3-quantised per matrix as
+the reference's FP8 path quantises them, bf16 activations -- the precision that meets the
+north star's parity bounds (e4m3 activations cannot: see tests/test_precision.py). Each GPU holds
+a full weight replica and evaluates its own batch (weak scaling, no collective on the data path;
+a gloo process group on the host carries only the barrier and the max over ranks).
 
-    python bench.py [--gpus N --steps K --warmup W --batch B --net small|nano --precision fp8|fp8w|bf16]
+    python bench.py [--gpus N --steps K --warmup W --batch B --net small|nano --precision fp8w|fp8|bf16]
     python bench.py --impl reference ...   # the reference's CPU backend (its C restatement) on host cores
 
 Prints one JSON line (rank 0).
@@ -28,13 +31,6 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
-# stdout carries exactly one JSON line: keep NCCL's version banner off it.
-if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-    os.environ["NCCL_DEBUG"] = "WARN"
-# NCCL writes its log (the version line included, at WARN) to stdout unless told otherwise; stdout
-# carries only the JSON line.
-os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
-
 # DRAM bytes (read + write) of all GEMM launches of one forward pass, per position: ncu
 # dram__bytes_read.sum + dram__bytes_write.sum summed over the 49 GEMM launches of one pass of
 # `bench.py --batch 1024 --precision fp8` (the traffic grows with the rows; the weights are
@@ -53,7 +49,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--net", choices=["small", "nano"], default="small")
     ap.add_argument("--batch", type=int, default=4096, help="positions per GPU per step")
-    ap.add_argument("--precision", choices=["fp8", "fp8w", "bf16"], default="fp8")
+    ap.add_argument("--precision", choices=["fp8w", "fp8", "bf16"], default="fp8w")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fp8-peak", action="store_true",
@@ -66,6 +62,7 @@ def parse_args():
     ap.add_argument("--nodes", type=int, default=100_000)
     ap.add_argument("--positions", type=int, default=1 << 20)
     ap.add_argument("--chunk", type=int, default=8192)
+    ap.add_argument("--scan", action="store_true", help="puct / wholebox: measure at 1, 2, 4, ... up to --gpus GPUs")
     return ap.parse_args()
 
 
@@ -98,7 +95,12 @@ def flops_per_eval(arch) -> float:
 
 
 # ---- CPU baseline: the oracle (C restatement of src/net/cpu.rs) on the host cores ---------
-def cpu_baseline(args, arch, w, seconds: float) -> dict:
+def cpu_baseline(args, arch, w, seconds: float, gpu_evaluate=None) -> dict:
+    """The oracle on all host threads over a bounded sample of the workload. With `gpu_evaluate`
+    (boards, legal -> priors, wdl through the GPU evaluator), the oracle's outputs for the sample are
+    also the checker of the GPU's on the same positions: the returned "parity" holds the north
+    star's figures (max |prior| and |WDL| differences over legal slots, max KL, tie-aware and raw
+    argmax agreement)."""
     import oracle
     from marina_b200 import chess, weights
 
@@ -106,19 +108,37 @@ def cpu_baseline(args, arch, w, seconds: float) -> dict:
     wq = weights.fp8_weights(w) if args.precision != "bf16" else w
     net = oracle.OracleNetwork(arch, wq, threads=threads)
     # every thread gets at least one 512-row slice (src/net/cpu.rs:352 slices rows the same way)
-    chunk = min(max(8 * threads, 16), 2048)
-    boards, legal, _, _ = chess.random_positions(4242, chunk)
+    chunk = min(max(16 * threads, 16), 2048)
+    boards, legal, counts, _ = chess.random_positions(4242, chunk)
     net.evaluate(boards[:2], legal[:2])  # warm
     done, t0 = 0, time.perf_counter()
     while True:
-        net.evaluate(boards, legal)
+        ref_p, ref_w = net.evaluate(boards, legal)
         done += chunk
         el = time.perf_counter() - t0
         if el >= seconds or el > 0 and done / el * seconds < chunk * 0.5:
             break
     el = time.perf_counter() - t0
-    return {"value": done / el, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{done} positions of the {args.net} config ({chunk}-position batches) in {el:.1f} s"}
+    out = {"value": done / el, "unit": UNIT, "cores": threads, "kind": "port",
+           "sample": f"{done} positions of the {args.net} config ({chunk}-position batches) in {el:.1f} s"}
+    if gpu_evaluate is not None:
+        out["parity"] = parity(*gpu_evaluate(boards, legal), ref_p, ref_w, counts)
+    return out
+
+
+def parity(priors, wdl, ref_p, ref_w, counts) -> dict:
+    """The north star's parity figures of GPU outputs against the oracle's on the same positions."""
+    tie = 2e-4
+    n = len(counts)
+    prior = max(float(np.abs(priors[p, :c] - ref_p[p, :c]).max()) for p, c in enumerate(counts))
+    kl = max(float(np.sum(ref_p[p, :c] * (np.log(np.maximum(ref_p[p, :c], 1e-30))
+                                          - np.log(np.maximum(priors[p, :c], 1e-30))))) for p, c in enumerate(counts))
+    raw = float(np.mean([np.argmax(priors[p, :c]) == np.argmax(ref_p[p, :c]) for p, c in enumerate(counts)]))
+    tied = float(np.mean([ref_p[p, np.argmax(priors[p, :c])] >= ref_p[p, :c].max() - tie
+                          for p, c in enumerate(counts)]))
+    return {"positions": n, "prior_max_abs": prior, "wdl_max_abs": float(np.abs(wdl - ref_w).max()), "kl_max": kl,
+            "argmax_tie_aware": tied, "argmax_raw": raw, "tie": tie,
+            "bounds": {"prior": 3e-2, "wdl": 2e-2, "kl": 1e-2, "argmax": 0.99}}
 
 
 def run_reference(args):
@@ -155,14 +175,15 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def reduce_max(v: float, world: int, device) -> float:
-    """The maximum of `v` over all ranks of the default process group (identity when alone)."""
+def reduce_max(v: float, world: int) -> float:
+    """The maximum of `v` over all ranks of the default (gloo, host) process group (identity when
+    alone)."""
     if world == 1:
         return v
     import torch
     import torch.distributed as dist
 
-    t = torch.tensor([v], device=device, dtype=torch.float64)
+    t = torch.tensor([v], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -275,14 +296,16 @@ def run_ours(args):
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        # The ranks share nothing on the data path; a host (gloo) group carries the barrier and
+        # the max over ranks of the device timings.
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
 
     def barrier():
         if world > 1:
             dist.barrier()
 
     def max_over_ranks(v: float) -> float:
-        return reduce_max(v, world, dev)
+        return reduce_max(v, world)
 
     arch, w = load_net(args.net)
     B = args.batch
@@ -395,7 +418,9 @@ def run_ours(args):
             "describe": net.describe(),
         }
         if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(args, arch, w, args.cpu_seconds)
+            line["cpu_baseline"] = cpu_baseline(args, arch, w, args.cpu_seconds,
+                                                gpu_evaluate=lambda b, lg: net.evaluate_packed(b, lg))
+            line["config"]["parity"] = line["cpu_baseline"]["parity"]
         print(json.dumps(line), flush=True)
     net.close()
     if world > 1:
@@ -451,6 +476,21 @@ def run_sweep(args):
     net.close()
 
 
+def gpu_counts(args) -> list[int]:
+    """The GPU counts a puct / wholebox run measures: --gpus alone, or with --scan 1, 2, 4, ... up to it."""
+    if not args.scan:
+        return [args.gpus]
+    out, n = [], 1
+    while n < args.gpus:
+        out.append(n)
+        n *= 2
+    return out + [args.gpus]
+
+
+def peaks() -> dict:
+    return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+
+
 # ---- configs[3]: batched PUCT nodes/s on N GPUs (one process, per-GPU evaluator threads) -----
 def run_puct(args):
     import ctypes
@@ -459,76 +499,93 @@ def run_puct(args):
     from marina_b200.network import B200Network
 
     arch, w = load_net(args.net)
-    n_gpus = args.gpus
     workers = 2  # two gathering threads per GPU: one gathers while the other's batch is evaluated
-    roots_per_worker = -(-args.roots // (n_gpus * workers))
+    counts = gpu_counts(args)
+    roots_per_worker = -(-args.roots // workers)  # the most any GPU's workers hold (one GPU)
     nets = [B200Network(arch, w, device=g, max_batch=roots_per_worker * 256, precision=args.precision)
-            for g in range(n_gpus)]
+            for g in range(max(counts))]
     _, _, _, fens = chess.random_positions(1, args.roots, 0, 80, fens=True)
     roots = [chess.from_fen(f) for f in fens]
     fn = ctypes.cast(_lib.load().mrn_evaluate, ctypes.c_void_p).value
-    evaluators = [(fn, net._ctx.value) for net in nets]
-    warm, _ = search.search(roots[:max(1, n_gpus)], 2000, evaluators, workers)  # graphs, clocks
-    per_root, total = search.search(roots, args.nodes, evaluators, workers, search.default_params(256))
-    print(json.dumps({"mode": "puct", "net": args.net, "precision": args.precision, "gpus": n_gpus,
-                      "roots": args.roots, "node_limit": args.nodes, "leaf_batch": 256,
-                      "nodes": total["nodes"], "seconds": total["seconds"],
-                      "nodes_per_s": total["nodes"] / total["seconds"],
-                      "network_evals": total["network_evals"], "collisions": total["collisions"],
-                      "max_depth": total["max_depth"], "workers_per_gpu": workers,
-                      "describe": nets[0].describe()}), flush=True)
+    for n_gpus in counts:
+        evaluators = [(fn, net._ctx.value) for net in nets[:n_gpus]]
+        search.search(roots[:max(1, 2 * n_gpus)], 2000, evaluators, workers)  # graphs, clocks
+        with ClockSampler(0) as clocks:
+            per_root, total = search.search(roots, args.nodes, evaluators, workers, search.default_params(256))
+        print(json.dumps({"mode": "puct", "net": args.net, "precision": args.precision, "gpus": n_gpus,
+                          "roots": args.roots, "node_limit": args.nodes, "leaf_batch": 256,
+                          "nodes": total["nodes"], "seconds": total["seconds"],
+                          "nodes_per_s": total["nodes"] / total["seconds"],
+                          "network_evals": total["network_evals"], "batches": total["batches"],
+                          "evals_per_batch": total["network_evals"] / max(1, total["batches"]),
+                          "collisions": total["collisions"], "max_depth": total["max_depth"],
+                          "workers_per_gpu": workers, "clocks_gpu0": clocks.summary(),
+                          "describe": nets[0].describe()}), flush=True)
     for net in nets:
         net.close()
 
 
 # ---- whole-box throughput, 1M positions in 8192-position chunks over N GPUs -----
 def run_wholebox(args):
-    from concurrent.futures import ThreadPoolExecutor
-
+    """1,048,576 positions in chunks of --chunk positions through the multi-device
+    evaluator (`mrn_group_evaluate`: every chunk is cut into one contiguous shard per GPU, evaluated
+    at the same time by the library's per-device threads), host buffers pinned. Beside it: the
+    fraction of the box's roofline (tensor-bound `small`: GEMM FLOPs at the measured bf16 peak, x2
+    for e4m3; HBM-bound `nano`: the layer-boundary bytes at the measured copy bandwidth) and the
+    oracle on all host cores on a bounded sample."""
     import torch
 
     from marina_b200 import chess
-    from marina_b200.network import B200Network
+    from marina_b200.network import GroupNetwork
 
     arch, w = load_net(args.net)
-    n_gpus, chunk = args.gpus, args.chunk
+    chunk = args.chunk
     t0 = time.perf_counter()
     boards, legal, _, _ = chess.random_positions(1, args.positions, 0, 80)
     gen_s = time.perf_counter() - t0
-    nets = [B200Network(arch, w, device=g, max_batch=chunk, precision=args.precision) for g in range(n_gpus)]
-    chunks = [(a, min(a + chunk, args.positions)) for a in range(0, args.positions, chunk)]
-
-    def shard(g):
-        # pinned staging per GPU: the host->device copies run at full PCIe speed
-        hb = torch.empty((chunk, 66), dtype=torch.uint8).pin_memory().numpy()
-        hl = torch.empty((chunk, 224), dtype=torch.int32).pin_memory().numpy()
-        hp = torch.empty((chunk, 224)).pin_memory().numpy()
-        hw = torch.empty((chunk, 3)).pin_memory().numpy()
-        nets[g].evaluate_packed(boards[:chunk], legal[:chunk], hp, hw)  # warm the bucket's graph
-        return hb, hl, hp, hw
-
-    with ThreadPoolExecutor(n_gpus) as pool:
-        bufs = list(pool.map(shard, range(n_gpus)))
-
-        def work(g):
-            hb, hl, hp, hw = bufs[g]
-            checksum = 0.0
-            for a, b in chunks[g::n_gpus]:
-                n = b - a
-                hb[:n], hl[:n] = boards[a:b], legal[a:b]
-                nets[g].evaluate_packed(hb[:n], hl[:n], hp[:n], hw[:n])
-                checksum += float(hw[:n, 0].sum())
-            return checksum
-
-        t0 = time.perf_counter()
-        sums = list(pool.map(work, range(n_gpus)))
-        el = time.perf_counter() - t0
-    print(json.dumps({"mode": "wholebox", "net": args.net, "precision": args.precision, "gpus": n_gpus,
-                      "positions": args.positions, "chunk": chunk, "seconds": el, "evals_per_s": args.positions / el,
-                      "path": "mrn_evaluate per chunk (host pinned buffers, H2D + graph + D2H), one thread per GPU",
-                      "input_generation_s": gen_s, "wdl_win_sum": sum(sums)}), flush=True)
-    for net in nets:
-        net.close()
+    hb = torch.from_numpy(boards).pin_memory().numpy()
+    hl = torch.from_numpy(legal).pin_memory().numpy()
+    hp = torch.empty((args.positions, 224)).pin_memory().numpy()
+    hw = torch.empty((args.positions, 3)).pin_memory().numpy()
+    pk = peaks()
+    bf16 = pk.get("bf16_tflops_sustained") or 1400.0
+    gemm_peak = (2 if args.precision == "fp8" else 1) * bf16 * 1e12
+    hbm = (pk.get("hbm_gbs") or 6650.0) * 1e9
+    d, L, ff, T = arch.d_model, arch.n_layers, arch.d_ff, arch.tokens
+    ab = 1 if args.precision == "fp8" else 2
+    # layer-boundary algorithmic bytes per position: per layer x (f16) read by 2 LayerNorms and
+    # read+written by 2 residual GEMMs; h written by 2 LNs and read by QKV/FFN1; qkv (bf16) written
+    # and read; attention out written and read; the FFN hidden written and read.
+    bytes_per_eval = T * L * (2 * d * 2 + 2 * 2 * d * 2 + 2 * 2 * d * ab + 2 * 3 * d * 2 + 2 * d * ab + 2 * ff * ab)
+    flops = flops_per_eval(arch)
+    cpu = cpu_baseline(args, arch, w, args.cpu_seconds) if not args.no_cpu_baseline else None
+    for n_gpus in gpu_counts(args):
+        group = GroupNetwork(arch, w, list(range(n_gpus)), max_batch=chunk, precision=args.precision)
+        group.evaluate_packed(hb[:chunk], hl[:chunk], hp[:chunk], hw[:chunk])  # graphs, clocks
+        with ClockSampler(0) as clocks:
+            t0 = time.perf_counter()
+            for a in range(0, args.positions, chunk):
+                b = min(a + chunk, args.positions)
+                group.evaluate_packed(hb[a:b], hl[a:b], hp[a:b], hw[a:b])
+            el = time.perf_counter() - t0
+        value = args.positions / el
+        tensor_frac = value * flops / (n_gpus * gemm_peak)
+        hbm_frac = value * bytes_per_eval / (n_gpus * hbm)
+        line = {"mode": "wholebox", "net": args.net, "precision": args.precision, "gpus": n_gpus,
+                "positions": args.positions, "chunk": chunk, "seconds": el, "evals_per_s": value,
+                "roofline": {"bound": "tensor" if args.net == "small" else "hbm",
+                             "frac": tensor_frac if args.net == "small" else hbm_frac,
+                             "tensor_frac": tensor_frac, "hbm_frac": hbm_frac,
+                             "flops_per_eval": flops, "layer_boundary_bytes_per_eval": bytes_per_eval,
+                             "peaks": {"gemm_tflops": gemm_peak / 1e12, "hbm_gbs": hbm / 1e9,
+                                       "source": "MEASURED_PEAKS.json (bf16 sustained; x2 for e4m3)"}},
+                "path": "mrn_group_evaluate per chunk (pinned host buffers; per GPU: H2D + graph + D2H)",
+                "input_generation_s": gen_s, "clocks_gpu0": clocks.summary(), "describe": group.describe()}
+        if cpu:
+            line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            line["gpu_over_cpu"] = value / cpu["value"]
+        print(json.dumps(line), flush=True)
+        group.close()
 
 
 def run_gemm(args):

@@ -9,10 +9,12 @@ first has an oracle prior more than TIE (2e-4, the reference's own fp32-vs-fp32 
 tolerance, src/net/verify.rs:62-66) below the oracle's best. Random-init policies are close
 to uniform and a few percent of positions have top-2 prior margins below 1e-4, which no
 implementation with a different summation order can resolve; the raw agreement is printed
-beside it. The criterion applies to the bf16-activation precisions ("bf16", "fp8w"); e4m3
-activations ("fp8", the reference's FP8 path) carry ~3.6% rms rounding noise per GEMM input,
-which reorders near-uniform random-init policies on roughly one position in ten, so that mode
-is held to the WDL / prior / KL bounds and a looser argmax floor."""
+beside it. The >= 99% criterion applies to the bf16-activation precisions ("bf16", "fp8w", the
+default). e4m3 activations ("fp8", the reference's FP8 path) cannot meet it on these policies at
+any scale granularity (tests/test_precision.py): their argmax floor is what the format itself
+reaches -- the float32 simulation of the same e4m3 rounding (torch_reference.forward_quantised,
+run on the GPU) on the same positions -- less FP8_SLACK, so the kernels are held to adding no
+error of their own."""
 
 import threading
 
@@ -26,7 +28,7 @@ from marina_b200.network import B200Network, NetworkError, ShardedNetwork
 pytestmark = pytest.mark.gpu
 
 WDL_TOL, PRIOR_TOL, KL_TOL, ARGMAX_MIN = 2e-2, 3e-2, 1e-2, 0.99
-ARGMAX_MIN_FP8 = 0.80
+FP8_SLACK = 0.03
 TIE = 2e-4
 
 
@@ -52,13 +54,36 @@ def compare(priors, wdl, ref_priors, ref_wdl, counts):
                 oracle_margin_lt_tie=float(np.mean(np.array(margins) < TIE)), pad_zero=pad_zero, sums=sums)
 
 
-def check(m, precision):
+def e4m3_format_agreement(arch, w, boards, legal, counts, ref_p):
+    """Tie-aware argmax agreement with the oracle's priors `ref_p` of the float32 simulation of the
+    fp8 precision's own rounding (e4m3 weights, the four GEMM inputs e4m3 with the card's static
+    scales, f16 residual stream), on the GPU."""
+    from tests import torch_reference as tr
+
+    policy, _ = tr.forward_quantised(arch, weights.fp8_weights(w), boards,
+                                     {s: "tensor" for s in ("n1", "at", "n2", "ge")}, device="cuda")
+    return tr.agreement(tr.priors_from_logits(policy, legal), ref_p, counts, TIE)[0]
+
+
+def check(m, precision, format_agreement=None):
+    """The north star's bounds. For "fp8" the argmax floor is `format_agreement` (what e4m3
+    activations reach on these positions, see e4m3_format_agreement) less FP8_SLACK."""
+    argmax_min = ARGMAX_MIN
+    if precision == "fp8":
+        assert format_agreement is not None, "fp8 checks need the e4m3 format's own agreement"
+        argmax_min = format_agreement - FP8_SLACK
+        m = m | {"e4m3_format_argmax": format_agreement}
     print(precision, m)
     assert m["wdl"] <= WDL_TOL, m
     assert m["prior"] <= PRIOR_TOL, m
     assert m["kl"] <= KL_TOL, m
-    assert m["argmax"] >= (ARGMAX_MIN_FP8 if precision == "fp8" else ARGMAX_MIN), m
+    assert m["argmax"] >= argmax_min, m
     assert m["pad_zero"] and m["sums"] < 1e-4, m
+
+
+def check_against(priors, wdl, ref_p, ref_w, counts, precision, arch, w, boards, legal):
+    fmt = e4m3_format_agreement(arch, w, boards, legal, counts, ref_p) if precision == "fp8" else None
+    check(compare(priors, wdl, ref_p, ref_w, counts), precision, fmt)
 
 
 @pytest.fixture(scope="module")
@@ -83,7 +108,7 @@ def test_nano_golden_config(nano_setup, precision):
         ref_p, ref_w = oracle.OracleNetwork(arch, weights.fp8_weights(w), threads=8).evaluate(boards, legal)
     net = B200Network(arch, w, max_batch=64, precision=precision)
     priors, wdl = net.evaluate_packed(boards, legal)
-    check(compare(priors, wdl, ref_p, ref_w, counts), precision)
+    check_against(priors, wdl, ref_p, ref_w, counts, precision, arch, w, boards, legal)
 
 
 @pytest.fixture(scope="module")
@@ -104,7 +129,7 @@ def test_small_config_batch_256(small_setup, precision):
     ref_p, ref_w = ref if precision == "bf16" else ref_q
     net = B200Network(arch, w, max_batch=256, precision=precision)
     priors, wdl = net.evaluate_packed(boards, legal)
-    check(compare(priors, wdl, ref_p, ref_w, counts), precision)
+    check_against(priors, wdl, ref_p, ref_w, counts, precision, arch, w, boards, legal)
 
 
 def test_f16_priors_are_the_f32_priors_rounded(small_setup):
@@ -121,7 +146,8 @@ def test_f16_priors_are_the_f32_priors_rounded(small_setup):
         assert p16.dtype == np.float16 and p16.shape == p32.shape
         assert np.array_equal(p16, p32.astype(np.float16))
         assert np.array_equal(w16, w32)
-    check(compare(p16.astype(np.float32), w16, ref_q[0], ref_q[1], counts) | {"sums": 0.0}, "fp8")
+    check(compare(p16.astype(np.float32), w16, ref_q[0], ref_q[1], counts) | {"sums": 0.0}, "fp8",
+          e4m3_format_agreement(arch, w, boards, legal, counts, ref_q[0]))
     sums = [abs(float(p16[p, :c].astype(np.float64).sum()) - 1) for p, c in enumerate(counts)]
     assert max(sums) < 224 * 2.0 ** -11, max(sums)
     n = len(counts)
@@ -148,7 +174,7 @@ def test_argmax_agreement_on_1024_positions(net, precision):
     ref_p, ref_w = oracle.OracleNetwork(arch, weights.fp8_weights(w) if precision != "bf16" else w,
                                         threads=16).evaluate(boards, legal)
     priors, wdl = B200Network(arch, w, max_batch=1024, precision=precision).evaluate_packed(boards, legal)
-    check(compare(priors, wdl, ref_p, ref_w, counts), precision)
+    check_against(priors, wdl, ref_p, ref_w, counts, precision, arch, w, boards, legal)
 
 
 @pytest.mark.parametrize("precision", ["bf16", "fp8w", "fp8"])
@@ -166,7 +192,7 @@ def test_tanh_gelu_card(precision):
     ref_p, ref_w = oracle.OracleNetwork(arch, weights.fp8_weights(w) if precision != "bf16" else w,
                                         threads=16).evaluate(boards, legal)
     priors, wdl = B200Network(arch, w, max_batch=128, precision=precision).evaluate_packed(boards, legal)
-    check(compare(priors, wdl, ref_p, ref_w, counts), precision)
+    check_against(priors, wdl, ref_p, ref_w, counts, precision, arch, w, boards, legal)
     # the erf card on the same weights differs, so the form is really applied
     erf_arch = card("nano")
     p_erf, _ = B200Network(erf_arch, w, max_batch=128, precision=precision).evaluate_packed(boards, legal)
@@ -348,7 +374,7 @@ def _check_plans_against_oracle(outs, net, precision):
     ref_p, ref_w = oracle.OracleNetwork(card(net), weights.fp8_weights(w) if precision != "bf16" else w,
                                         threads=16).evaluate(boards, legal)
     for out in outs.values():
-        check(compare(out["priors"], out["wdl"], ref_p, ref_w, counts), precision)
+        check_against(out["priors"], out["wdl"], ref_p, ref_w, counts, precision, card(net), w, boards, legal)
 
 
 @pytest.mark.parametrize("net,precision", [("small", "fp8w"), ("small", "bf16"), ("small", "fp8")])
