@@ -29,7 +29,7 @@ def _worker(rank, world, port, out):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     import bench
 
-    out[rank] = bench.reduce_max(float(10 * rank + 3), world, torch.device("cpu"))
+    out[rank] = bench.reduce_max(float(10 * rank + 3), world)
     dist.barrier()
     dist.destroy_process_group()
 
