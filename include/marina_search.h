@@ -59,6 +59,15 @@ MRC_API int mrs_search(const mrc_position* roots, int n_roots, uint64_t node_lim
                        mrs_eval_fn eval, void* const* contexts, int n_evaluators, int workers_per_evaluator,
                        mrs_summary* per_root, mrs_summary* total);
 
+/* `mrs_search`, also returning each root's children: `root_actions` and `root_visits` (both
+ * n_roots x 224, -1 / 0 past the root's children) receive per root the action index and the visit
+ * count of every child, in the root's move order -- the distribution the reference's search picks
+ * its move from (most visits), for comparing searches driven by different networks. */
+MRC_API int mrs_search_visits(const mrc_position* roots, int n_roots, uint64_t node_limit, const mrs_params* params,
+                              mrs_eval_fn eval, void* const* contexts, int n_evaluators, int workers_per_evaluator,
+                              mrs_summary* per_root, mrs_summary* total, int32_t* root_actions,
+                              uint32_t* root_visits);
+
 #ifdef __cplusplus
 }
 #endif

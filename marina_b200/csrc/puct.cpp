@@ -253,9 +253,11 @@ struct Worker {
 
 }  // namespace
 
-extern "C" MRC_API int mrs_search(const mrc_position* roots, int n_roots, uint64_t node_limit, const mrs_params* params,
-                                  mrs_eval_fn eval, void* const* contexts, int n_evaluators, int workers_per_evaluator,
-                                  mrs_summary* per_root, mrs_summary* total) {
+namespace {
+
+int search_all(const mrc_position* roots, int n_roots, uint64_t node_limit, const mrs_params* params, mrs_eval_fn eval,
+               void* const* contexts, int n_evaluators, int workers_per_evaluator, mrs_summary* per_root,
+               mrs_summary* total, int32_t* root_actions, uint32_t* root_visits) {
   if (!roots || n_roots <= 0 || !params || !eval || !contexts || n_evaluators <= 0 || workers_per_evaluator <= 0 ||
       params->batch <= 0 || params->batch > 4096)
     return -1;
@@ -297,6 +299,15 @@ extern "C" MRC_API int mrs_search(const mrc_position* roots, int n_roots, uint64
         best_action = mrc_encode_move(&s.root, s.nodes[c].mv);
       }
     s.sum.best_action = best_action;
+    if (root_actions && root_visits) {
+      int32_t* acts = root_actions + static_cast<size_t>(i) * kMaxLegal;
+      uint32_t* vis = root_visits + static_cast<size_t>(i) * kMaxLegal;
+      for (int k = 0; k < kMaxLegal; ++k) acts[k] = -1, vis[k] = 0;
+      for (uint32_t c = 0; c < root.count && c < static_cast<uint32_t>(kMaxLegal); ++c) {
+        acts[c] = mrc_encode_move(&s.root, s.nodes[root.first + c].mv);
+        vis[c] = s.nodes[root.first + c].visits;
+      }
+    }
     if (per_root) per_root[i] = s.sum;
     tot.nodes += s.sum.nodes;
     tot.network_evals += s.sum.network_evals;
@@ -310,4 +321,22 @@ extern "C" MRC_API int mrs_search(const mrc_position* roots, int n_roots, uint64
   tot.best_action = -1;
   if (total) *total = tot;
   return rc;
+}
+
+}  // namespace
+
+extern "C" MRC_API int mrs_search(const mrc_position* roots, int n_roots, uint64_t node_limit, const mrs_params* params,
+                                  mrs_eval_fn eval, void* const* contexts, int n_evaluators, int workers_per_evaluator,
+                                  mrs_summary* per_root, mrs_summary* total) {
+  return search_all(roots, n_roots, node_limit, params, eval, contexts, n_evaluators, workers_per_evaluator, per_root,
+                    total, nullptr, nullptr);
+}
+
+extern "C" MRC_API int mrs_search_visits(const mrc_position* roots, int n_roots, uint64_t node_limit,
+                                         const mrs_params* params, mrs_eval_fn eval, void* const* contexts,
+                                         int n_evaluators, int workers_per_evaluator, mrs_summary* per_root,
+                                         mrs_summary* total, int32_t* root_actions, uint32_t* root_visits) {
+  if (!root_actions || !root_visits) return -1;
+  return search_all(roots, n_roots, node_limit, params, eval, contexts, n_evaluators, workers_per_evaluator, per_root,
+                    total, root_actions, root_visits);
 }

@@ -34,15 +34,19 @@ def default_params(batch: int = 256) -> Params:
 
 
 def search(roots: list, node_limit: int, evaluators: list, workers_per_evaluator: int = 2,
-           params: Params | None = None):
+           params: Params | None = None, visits: bool = False):
     """Search every root position to `node_limit` nodes. `evaluators` is a list of
     (function pointer, context) pairs: the C function `mrn_evaluate` with an `mrn_ctx` per
-    GPU, or an `EVAL_FN` callback with any context. Returns (per-root summaries, total)."""
+    GPU, or an `EVAL_FN` callback with any context. Returns (per-root summaries, total); with
+    `visits`, each per-root summary also holds "root_visits": {action index: visits} over the
+    root's children (`mrs_search_visits`)."""
     lib = chess.load()
     if not hasattr(lib, "_mrs_ready"):
         lib.mrs_search.argtypes = [POINTER(chess.Position), c_int, c_uint64, POINTER(Params), c_void_p,
                                    POINTER(c_void_p), c_int, c_int, POINTER(Summary), POINTER(Summary)]
         lib.mrs_search.restype = c_int
+        lib.mrs_search_visits.argtypes = lib.mrs_search.argtypes + [POINTER(c_int32), POINTER(ctypes.c_uint32)]
+        lib.mrs_search_visits.restype = c_int
         lib._mrs_ready = True
     params = params or default_params()
     n = len(roots)
@@ -53,8 +57,19 @@ def search(roots: list, node_limit: int, evaluators: list, workers_per_evaluator
     ctxs = (c_void_p * len(evaluators))(*[c for _, c in evaluators])
     per_root = (Summary * n)()
     total = Summary()
-    rc = lib.mrs_search(arr, n, node_limit, ctypes.byref(params), c_void_p(fns.pop()), ctxs, len(evaluators),
-                        workers_per_evaluator, per_root, ctypes.byref(total))
+    if visits:
+        acts = (c_int32 * (n * 224))()
+        vis = (ctypes.c_uint32 * (n * 224))()
+        rc = lib.mrs_search_visits(arr, n, node_limit, ctypes.byref(params), c_void_p(fns.pop()), ctxs,
+                                   len(evaluators), workers_per_evaluator, per_root, ctypes.byref(total), acts, vis)
+    else:
+        rc = lib.mrs_search(arr, n, node_limit, ctypes.byref(params), c_void_p(fns.pop()), ctxs, len(evaluators),
+                            workers_per_evaluator, per_root, ctypes.byref(total))
     if rc != 0:
         raise RuntimeError(f"search failed (network error {rc})")
-    return [s.as_dict() for s in per_root], total.as_dict()
+    out = [s.as_dict() for s in per_root]
+    if visits:
+        for i, d in enumerate(out):
+            d["root_visits"] = {int(acts[i * 224 + k]): int(vis[i * 224 + k]) for k in range(224)
+                                if acts[i * 224 + k] >= 0}
+    return out, total.as_dict()

@@ -83,11 +83,22 @@ class Weights:
         return self.tensors[name].ctypes.data_as(POINTER(c_float))
 
     # ---- safetensors (the format `Weights::from_bytes` reads) -----------------------------
-    def to_safetensors(self) -> bytes:
+    def to_safetensors(self, dtype: str = "F32") -> bytes:
+        """The tensors as a safetensors file in `dtype` ("F32", "F16" or "BF16", rounded to nearest
+        even), the three element types `Weights::from_bytes` reads."""
         header, offset, blobs = {}, 0, []
         for name, _, _ in tensor_specs(self.arch):
-            data = self.tensors[name].astype("<f4").tobytes()
-            header[name] = {"dtype": "F32", "shape": list(self.tensors[name].shape), "data_offsets": [offset, offset + len(data)]}
+            t = self.tensors[name]
+            if dtype == "F32":
+                data = t.astype("<f4").tobytes()
+            elif dtype == "F16":
+                data = t.astype("<f2").tobytes()
+            elif dtype == "BF16":
+                bits = t.astype("<f4").view("<u4").astype(np.uint64)
+                data = ((bits + 0x7FFF + ((bits >> 16) & 1)) >> 16).astype("<u2").tobytes()
+            else:
+                raise WeightsError(f"cannot write dtype {dtype}")
+            header[name] = {"dtype": dtype, "shape": list(t.shape), "data_offsets": [offset, offset + len(data)]}
             offset += len(data)
             blobs.append(data)
         head = json.dumps(header, separators=(",", ":")).encode()
@@ -124,6 +135,52 @@ class Weights:
                 raise WeightsError(f"tensor {name} has dtype {dtype}; only F32, F16 and BF16 are read")
             tensors[name] = arr.reshape(info["shape"])
         return cls(arch, tensors)
+
+
+# Largest files read from a network directory (src/net/mod.rs:62-65).
+MAX_MODEL_JSON_BYTES = 16 << 20
+MAX_SAFETENSORS_BYTES = 4 << 30
+
+
+def _read_bounded(path, limit: int) -> bytes:
+    """A regular file read whole, refusing FIFOs / devices and anything larger than `limit`
+    (src/net/mod.rs:67-91)."""
+    import os
+    import stat
+
+    st = os.stat(path)
+    if not stat.S_ISREG(st.st_mode):
+        raise WeightsError(f"{path} is not a regular file")
+    if st.st_size > limit:
+        raise WeightsError(f"{path} is {st.st_size} bytes; at most {limit} are read")
+    with open(path, "rb") as f:
+        return f.read()
+
+
+def parse_dir(path) -> tuple[Architecture, "Weights"]:
+    """A network directory: `model.json` (the card) next to `model.safetensors` (the parameters
+    in F32, F16 or BF16), parsed with the reference's validation (`net::parse`,
+    src/net/mod.rs:118-160, model.rs:112-182, weights.rs:94-134)."""
+    from pathlib import Path
+
+    d = Path(path)
+    card = _read_bounded(d / "model.json", MAX_MODEL_JSON_BYTES)
+    try:
+        text = card.decode("utf-8")
+    except UnicodeDecodeError as e:
+        raise WeightsError(f"{d / 'model.json'}: {e}") from e
+    arch = Architecture.from_json(text)
+    return arch, Weights.from_safetensors(_read_bounded(d / "model.safetensors", MAX_SAFETENSORS_BYTES), arch)
+
+
+def write_dir(path, arch: Architecture, w: "Weights", dtype: str = "F32") -> None:
+    """Write `model.json` and `model.safetensors` (in `dtype`) into directory `path`."""
+    from pathlib import Path
+
+    d = Path(path)
+    d.mkdir(parents=True, exist_ok=True)
+    (d / "model.json").write_text(arch.to_json())
+    (d / "model.safetensors").write_bytes(w.to_safetensors(dtype))
 
 
 def random_init(arch: Architecture, seed: int = 0, std: float = 0.02, bias_std: float = 0.0,

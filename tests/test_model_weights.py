@@ -177,3 +177,29 @@ def test_other_architectures_do_not_load(tiny):
     arch, w = tiny
     with pytest.raises(WeightsError):
         Weights.from_safetensors(w.to_safetensors(), Architecture(64, 3, 2, 128))
+
+
+def test_network_directory_round_trip(tmp_path):
+    """write_dir / parse_dir: model.json + model.safetensors in F32 (exact), F16 and BF16 (rounded
+    to nearest even, as torch rounds), read back with the card's fields intact."""
+    import torch
+
+    arch = model.nano()
+    arch.fp8_amax = [[1.0, 2.0, 3.0, 4.0]] * arch.n_layers
+    w = weights.random_init(arch, seed=9, bias_std=0.1)
+    for dtype, tdt in (("F32", torch.float32), ("F16", torch.float16), ("BF16", torch.bfloat16)):
+        d = tmp_path / dtype
+        weights.write_dir(d, arch, w, dtype)
+        a2, w2 = weights.parse_dir(d)
+        assert a2.to_json() == arch.to_json()
+        for name in w.tensors:
+            want = torch.from_numpy(w[name]).to(tdt).to(torch.float32).numpy()
+            assert np.array_equal(w2[name], want), (dtype, name)
+
+
+def test_network_directory_errors(tmp_path):
+    with pytest.raises(FileNotFoundError):
+        weights.parse_dir(tmp_path / "missing")
+    (tmp_path / "model.json").mkdir()
+    with pytest.raises(weights.WeightsError, match="not a regular file"):
+        weights.parse_dir(tmp_path)

@@ -87,3 +87,18 @@ def test_a_network_error_stops_the_search_and_is_reported():
     with pytest.raises(RuntimeError, match="network error 6"):
         search.search([chess.startpos()], 1000, [(failing_net, None)], workers_per_evaluator=1,
                       params=search.default_params(16))
+
+
+def test_root_visit_distribution():
+    """mrs_search_visits returns every legal root move once, with the visits the search gave it:
+    they add up to the root's visits (one per node but the root's own), the most visited is the
+    best move, and one-thread searches repeat exactly."""
+    root = chess.from_fen("r3k2r/p1ppqpb1/bn2pnp1/3PN3/1p2P3/2N2Q1p/PPPBBPPP/R3K2R w KQkq - 0 1")
+    runs = [search.search([root], 1500, [(uniform_net, None)], workers_per_evaluator=1,
+                          params=search.default_params(32), visits=True)[0][0] for _ in range(2)]
+    a, b = runs
+    assert a["root_visits"] == b["root_visits"]
+    assert sorted(a["root_visits"]) == sorted(chess.legal_actions(root).tolist())
+    assert sum(a["root_visits"].values()) == a["nodes"] - 1
+    assert max(a["root_visits"], key=a["root_visits"].get) == a["best_action"] or \
+        a["root_visits"][a["best_action"]] == max(a["root_visits"].values())
