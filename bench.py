@@ -89,6 +89,20 @@ def workload_config(args, n_gpus: int) -> dict:
     }
 
 
+def algorithmic_bytes(arch, precision: str, positions: int) -> dict:
+    """DRAM bytes one pass's kernels of each memory-bound class must move at the layer-boundary
+    design: LayerNorm reads the f16 residual row and writes the GEMM operand row (2L - 1 launches);
+    attention reads Q, K, V (bf16) and writes its output row (L launches); the embedding writes x
+    and layer 0's h; the heads read the 65 rows of x, the legal slots and write the priors and the
+    value head's input."""
+    d, L, t = arch.d_model, arch.n_layers, arch.tokens
+    ab = 1 if precision == "fp8" else 2
+    rows = positions * t
+    return {"layernorm": (2 * L - 1) * rows * (2 * d + d * ab), "attention": L * rows * (6 * d + d * ab),
+            "embed": rows * (2 * d + d * ab) + positions * 66,
+            "heads": positions * (t * 2 * d + 224 * 4 * 2 + 2 * d)}
+
+
 def flops_per_eval(arch) -> float:
     d, ff, t, L = arch.d_model, arch.d_ff, arch.tokens, arch.n_layers
     return 2.0 * t * L * (4 * d * d + 2 * d * ff)
@@ -443,6 +457,9 @@ def run_sweep(args):
     torch.cuda.set_stream(stream)
     d_boards, d_legal = torch.from_numpy(boards).to(dev), torch.from_numpy(legal).to(dev)
     d_priors, d_wdl = torch.empty((max(sizes), 224), device=dev), torch.empty((max(sizes), 3), device=dev)
+    pk = peaks()
+    bf16_peak = (2 if args.precision == "fp8" else 1) * (pk.get("bf16_tflops_sustained") or 1400.0)
+    hbm_peak = pk.get("hbm_gbs") or 6650.0
     for b in sizes:
         step = lambda: net.evaluate_device(b, d_boards.data_ptr(), d_legal.data_ptr(), d_priors.data_ptr(),  # noqa: E731
                                            d_wdl.data_ptr(), stream.cuda_stream)
@@ -469,9 +486,14 @@ def run_sweep(args):
                            stream.cuda_stream)
         g = prof["gemm"]
         p50 = float(np.median(times))
+        nbytes = algorithmic_bytes(arch, args.precision, b)
+        hbm_gbs = {k: round(nbytes[k] / (prof[k]["ms"] / 1e3) / 1e9, 1) for k in nbytes if prof[k]["ms"] > 0}
         print(json.dumps({"mode": "sweep", "net": args.net, "precision": args.precision, "batch": b,
                           "latency_ms_p50": p50, "evals_per_s": b / (p50 / 1e3), "e2e_latency_ms": e2e_ms,
-                          "e2e_evals_per_s": b / (e2e_ms / 1e3), "e2e_f16_latency_ms": e2e_f16_ms, "gemm_tflops": g["flops"] / (g["ms"] / 1e3) / 1e12,
+                          "e2e_evals_per_s": b / (e2e_ms / 1e3), "e2e_f16_latency_ms": e2e_f16_ms,
+                          "gemm_tflops": g["flops"] / (g["ms"] / 1e3) / 1e12,
+                          "gemm_frac_of_bf16_sustained": g["flops"] / (g["ms"] / 1e3) / 1e12 / bf16_peak,
+                          "hbm_gbs": hbm_gbs, "hbm_frac": {k: round(v / hbm_peak, 3) for k, v in hbm_gbs.items()},
                           "kernel_ms": {k: round(v["ms"], 4) for k, v in prof.items()}}), flush=True)
     net.close()
 
