@@ -33,9 +33,9 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 # DRAM bytes (read + write) of all GEMM launches of one forward pass, per position: ncu
 # dram__bytes_read.sum + dram__bytes_write.sum summed over the 49 GEMM launches of one pass of
-# `bench.py --batch 1024 --precision fp8` (the traffic grows with the rows; the weights are
-# 19 MB a pass). Traffic of one full pass = this x the batch.
-GEMM_DRAM_BYTES_PER_EVAL = {("small", "fp8"): 7.60e6}
+# `bench.py --batch 4096` (fp8w), and of `bench.py --batch 1024 --precision fp8` for fp8. Traffic of
+# one full pass = this x the batch.
+GEMM_DRAM_BYTES_PER_EVAL = {("small", "fp8w"): 13.84e6, ("small", "fp8"): 7.60e6}
 METRIC = "small-net evals/sec per B200 and 8xB200 at batch 256-8192; PUCT nodes/sec"
 UNIT = "evals/s"
 L2_BYTES = 126 * 2 ** 20
