@@ -71,6 +71,11 @@ typedef enum mrn_precision {
    * calibration (src/net/model.rs:87-95, src/net/cuda/mod.rs:454-466), tcgen05
    * kind::f8f6f4. The reference's FP8 path (src/net/cuda/mod.rs:10-18). */
   MRN_PRECISION_FP8 = 2,
+  /* e4m3 weights as MRN_PRECISION_FP8; each activation v carried as two e4m3 terms with the
+   * same static scale s, hi = e4m3(v / s) and lo = e4m3(v / s - hi), and every GEMM K-step issued
+   * twice (hi and lo against the same weight codes) into one f32 accumulator: kind::f8f6f4 with
+   * about twice e4m3's significant bits per activation. Needs the calibration, like FP8. */
+  MRN_PRECISION_FP8_X2 = 3,
 } mrn_precision;
 
 typedef enum mrn_gelu {
@@ -89,8 +94,8 @@ typedef struct mrn_arch {
   int32_t tokens;             /* 65 in board mode */
   int32_t square_token_start; /* 1 in board mode */
   /* Per layer the four activation maxima (norm1 out, attention out, norm2 out, GELU out),
-   * [n_layers * 4], or NULL when the card has no calibration (then MRN_PRECISION_FP8 is
-   * refused). */
+   * [n_layers * 4], or NULL when the card has no calibration (then MRN_PRECISION_FP8 and
+   * MRN_PRECISION_FP8_X2 are refused). */
   const float* fp8_amax;
 } mrn_arch;
 

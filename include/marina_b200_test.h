@@ -20,9 +20,11 @@
 extern "C" {
 #endif
 
-/* One GEMM launch: out = epilogue(a[m,k] . b[n,k]^T * scale + bias). `fp8` selects e4m3
- * operands; `epilogue` is 0 bias->bf16, 1 GELU->bf16, 2 GELU->e4m3 (x inv_q), 3 residual
- * add into f16 `out`, 5 / 6 the tanh-form GELU into bf16 / e4m3. */
+/* One GEMM launch: out = epilogue(a[m,k] . b[n,k]^T * scale + bias). `fp8` selects the operand
+ * types: 0 bf16, 1 e4m3, 2 e4m3 weights with a two-term e4m3 `a` [m, 2k] (each row's k hi codes,
+ * then its k lo codes; the product is taken as (hi + lo) . b). `epilogue` is 0 bias->bf16,
+ * 1 GELU->bf16, 2 GELU->e4m3 (x inv_q), 3 residual add into f16 `out`, 5 / 6 the tanh-form GELU
+ * into bf16 / e4m3, 7 / 8 the erf / tanh GELU into two-term e4m3 (x inv_q) [m, 2n] (fp8 = 2). */
 MRN_TEST_API int mrn_test_gemm(int fp8, int epilogue, const void* a, const void* b, const float* bias, void* out,
                                int ldo, int m, int n, int k, float scale, float inv_q, int* status, void* stream);
 
@@ -38,12 +40,13 @@ MRN_TEST_API int mrn_test_gemm_wait_expiry(unsigned long long wait_limit_ns, con
 
 /* The attention kernel on its own: per (position, head), softmax(Q K^T / sqrt(hd)) V over the
  * position's 65 tokens from bf16 qkv [positions*65, 3d] (Q | K | V, head h at columns h*hd) into
- * out [positions*65, d], bf16, or with `e4m3` as e4m3 codes of the value * inv_q. */
+ * out [positions*65, d], bf16 (`e4m3` 0), e4m3 codes of the value * inv_q (1), or two-term e4m3
+ * codes of it (2: rows of 2d bytes, the d hi codes then the d lo codes). */
 MRN_TEST_API int mrn_test_attention(const void* qkv, void* out, int positions, int d, int heads, int e4m3,
                                     float inv_q, int* status, void* stream);
 
-/* The LayerNorm kernel on its own: out[rows,d] = LN(x) * gamma + beta from f16 x, as bf16, or
- * with `e4m3` as e4m3 codes of the value * inv_q. */
+/* The LayerNorm kernel on its own: out[rows,d] = LN(x) * gamma + beta from f16 x, as bf16
+ * (`e4m3` 0), e4m3 codes of the value * inv_q (1) or two-term e4m3 codes of it (2, as above). */
 MRN_TEST_API int mrn_test_layernorm(const void* x, const float* gamma, const float* beta, float eps, int e4m3,
                                     float inv_q, void* out, int rows, int d, void* stream);
 

@@ -24,7 +24,9 @@ WDL = 3
 PRECISION_BF16 = 0
 PRECISION_FP8_WEIGHTS = 1
 PRECISION_FP8 = 2
-PRECISIONS = {"bf16": PRECISION_BF16, "fp8w": PRECISION_FP8_WEIGHTS, "fp8": PRECISION_FP8}
+PRECISION_FP8_X2 = 3
+PRECISIONS = {"bf16": PRECISION_BF16, "fp8w": PRECISION_FP8_WEIGHTS, "fp8": PRECISION_FP8,
+              "fp8x2": PRECISION_FP8_X2}
 
 PROFILE_SLOTS = ("embed", "layernorm", "gemm", "attention", "heads")
 

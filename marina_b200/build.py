@@ -33,7 +33,7 @@ CHESS_LIB = PKG / "libmarina_chess.so"
 
 CUDA_SOURCES = ["gemm.cu", "kernels.cu", "attention.cu", "runtime.cu", "static_forward.cu", "group.cpp"]
 TEST_SOURCES = ["gemm.cu", "kernels.cu", "attention.cu", "api_test.cu"]
-CUDA_HEADERS = ["ptx.cuh", "rows.cuh", "gemm.cuh", "gemm.h", "tmap.h", "kernels.cuh", "launch.h", "runtime.h"]
+CUDA_HEADERS = ["ptx.cuh", "rows.cuh", "e4m3x2.cuh", "gemm.cuh", "gemm.h", "tmap.h", "kernels.cuh", "launch.h", "runtime.h"]
 CHESS_SOURCES = ["chess.cpp", "puct.cpp"]
 
 NVCC_FLAGS = [

@@ -61,7 +61,9 @@ MRN_TEST_API int mrn_test_gemm(int fp8, int epilogue, const void* a, const void*
   args.m = m;
   args.n = n;
   args.k = k;
+  if (fp8 < 0 || fp8 > 2) return fail("fp8 must be 0 (bf16), 1 (e4m3) or 2 (two-term e4m3 A)");
   args.fp8 = fp8 != 0;
+  args.x2 = fp8 == 2;
   args.epi = static_cast<mrn::Epilogue>(epilogue);
   args.out = out;
   args.ldo = ldo;
@@ -121,7 +123,8 @@ MRN_TEST_API int mrn_test_attention(const void* qkv, void* out, int positions, i
     prepared = true;
   }
   if (heads <= 0 || d % heads != 0) return fail("attention: d must be a multiple of heads");
-  const mrn::AttentionParams ap{qkv, out, e4m3 ? mrn::ActType::kE4m3 : mrn::ActType::kBf16, inv_q, 65, d, heads, status};
+  if (e4m3 < 0 || e4m3 > 2) return fail("e4m3 must be 0, 1 or 2");
+  const mrn::AttentionParams ap{qkv, out, static_cast<mrn::ActType>(e4m3), inv_q, 65, d, heads, status};
   const cudaError_t e = mrn::launch_attention(ap, positions, d / heads, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     snprintf(g_test_error, sizeof(g_test_error), "attention launch: %s", cudaGetErrorString(e));
@@ -132,7 +135,8 @@ MRN_TEST_API int mrn_test_attention(const void* qkv, void* out, int positions, i
 
 MRN_TEST_API int mrn_test_layernorm(const void* x, const float* gamma, const float* beta, float eps, int e4m3,
                                     float inv_q, void* out, int rows, int d, void* stream) {
-  const mrn::NormParams np{gamma, beta, eps, out, e4m3 ? mrn::ActType::kE4m3 : mrn::ActType::kBf16, inv_q};
+  if (e4m3 < 0 || e4m3 > 2) return fail("e4m3 must be 0, 1 or 2");
+  const mrn::NormParams np{gamma, beta, eps, out, static_cast<mrn::ActType>(e4m3), inv_q};
   const cudaError_t e = mrn::launch_layernorm(static_cast<const __half*>(x), np, rows, d, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     snprintf(g_test_error, sizeof(g_test_error), "layernorm launch: %s", cudaGetErrorString(e));

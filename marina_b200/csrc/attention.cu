@@ -23,6 +23,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 
+#include "e4m3x2.cuh"
 #include "kernels.cuh"
 #include "launch.h"
 #include "ptx.cuh"
@@ -80,7 +81,7 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
   return static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
 }
 
-template <int HD, int T, bool E4M3>
+template <int HD, int T, int OUT>  // OUT: 0 bf16, 1 e4m3, 2 two-term e4m3 (hi | lo rows)
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap map_qkv, AttentionParams p, int items) {
   constexpr int RB = HD * 2;                  // bytes per staged row
@@ -238,7 +239,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
       // Normalised strip -> this warp's Q rows (no longer read; own XOR layout: chunk ^ row)
       // -> 16-byte global stores of the rows < T.
-      constexpr int kOutRow = HD * (E4M3 ? 1 : 2);  // output bytes per row
+      constexpr int kOutRow = HD * (OUT == 1 ? 1 : 2);  // output bytes per row (x2: HD hi, then HD lo)
       constexpr int kChunks = kOutRow / 16;
       const float inv0 = 1.f / l0, inv1 = 1.f / l1;
       uint8_t* so = sq + r0 * RB;  // 16 rows x RB bytes
@@ -248,7 +249,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int nt = 0; nt < HD / 8; ++nt) {
         const int col = nt * 8 + 2 * tq;
-        if constexpr (E4M3) {
+        if constexpr (OUT == 2) {
+          uint16_t hi, lo;
+          split_e4m3x2(make_float2(o[nt][0] * inv0 * p.inv_q, o[nt][1] * inv0 * p.inv_q), hi, lo);
+          *reinterpret_cast<uint16_t*>(at(g, col)) = hi;
+          *reinterpret_cast<uint16_t*>(at(g, HD + col)) = lo;
+          split_e4m3x2(make_float2(o[nt][2] * inv1 * p.inv_q, o[nt][3] * inv1 * p.inv_q), hi, lo);
+          *reinterpret_cast<uint16_t*>(at(g + 8, col)) = hi;
+          *reinterpret_cast<uint16_t*>(at(g + 8, HD + col)) = lo;
+        } else if constexpr (OUT == 1) {
           *reinterpret_cast<__nv_fp8x2_storage_t*>(at(g, col)) = __nv_cvt_float2_to_fp8x2(
               make_float2(o[nt][0] * inv0 * p.inv_q, o[nt][1] * inv0 * p.inv_q), __NV_SATFINITE, __NV_E4M3);
           *reinterpret_cast<__nv_fp8x2_storage_t*>(at(g + 8, col)) = __nv_cvt_float2_to_fp8x2(
@@ -266,8 +275,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int row = r0 + rr;
         if (row < T) {
           const uint4 v = *reinterpret_cast<const uint4*>(at(rr, c * 16));
-          uint8_t* dst = static_cast<uint8_t*>(p.out) +
-                         ((static_cast<size_t>(pos) * T + row) * d + head * HD) * (E4M3 ? 1 : 2) + c * 16;
+          const size_t grow = static_cast<size_t>(pos) * T + row;
+          uint8_t* dst;
+          if constexpr (OUT == 2)  // hi chunks to the head's columns, lo chunks d bytes further on
+            dst = static_cast<uint8_t*>(p.out) + grow * 2 * d + head * HD + (c * 16 < HD ? c * 16 : d + c * 16 - HD);
+          else
+            dst = static_cast<uint8_t*>(p.out) + (grow * d + head * HD) * (OUT == 1 ? 1 : 2) + c * 16;
           *reinterpret_cast<uint4*>(dst) = v;
         }
       }
@@ -288,16 +301,21 @@ template <int HD, int T>
 cudaError_t launch_attention_t(const AttentionParams& p, const CUtensorMap& map, int grid, int items, cudaStream_t s) {
   constexpr int smem = attention_smem<HD, T>();
   if (p.out_type == ActType::kE4m3)
-    return launch_kernel(attention_kernel<HD, T, true>, dim3(grid), dim3(kAttnThreads), smem, s, map, p, items);
-  return launch_kernel(attention_kernel<HD, T, false>, dim3(grid), dim3(kAttnThreads), smem, s, map, p, items);
+    return launch_kernel(attention_kernel<HD, T, 1>, dim3(grid), dim3(kAttnThreads), smem, s, map, p, items);
+  if (p.out_type == ActType::kE4m3x2)
+    return launch_kernel(attention_kernel<HD, T, 2>, dim3(grid), dim3(kAttnThreads), smem, s, map, p, items);
+  return launch_kernel(attention_kernel<HD, T, 0>, dim3(grid), dim3(kAttnThreads), smem, s, map, p, items);
 }
 
 template <int HD, int T>
 cudaError_t prepare_attention_t() {
   constexpr int smem = attention_smem<HD, T>();
-  cudaError_t e = cudaFuncSetAttribute(attention_kernel<HD, T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = cudaFuncSetAttribute(attention_kernel<HD, T, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(attention_kernel<HD, T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if ((e = cudaFuncSetAttribute(attention_kernel<HD, T, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) !=
+      cudaSuccess)
+    return e;
+  return cudaFuncSetAttribute(attention_kernel<HD, T, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
 // The qkv tensor as TMA sees it: [rows, 3d] bf16, boxes of 80 rows x head_dim columns with the

@@ -11,53 +11,66 @@ namespace mrn {
 
 namespace {
 
-template <int BN, class Epi>
-using ShapeOf = GemmShape<BN, Epi::kWarps, Epi::kOutBytes>;
+template <int BN, class Epi, bool X2>
+using ShapeOf = GemmShape<BN, Epi::kWarps, Epi::kOutBytes, X2 ? 2 : 1>;
 
-template <int BN, bool FP8, class Epi>
+template <class Epi, bool X2>
+using PairShapeOf = PairShape<Epi::kOutBytes, Epi::kWarps, X2 ? 2 : 1>;
+
+template <int BN, bool FP8, bool X2, class Epi>
 cudaError_t launch_one(const GemmPlan& p, const Epi& epi, cudaStream_t stream) {
-  return launch_kernel(gemm_tc_kernel<BN, FP8, Epi>, dim3(p.grid), dim3(ShapeOf<BN, Epi>::kThreads),
-                       ShapeOf<BN, Epi>::kSmemBytes, stream, p.map_a, p.map_b, p.map_out, epi, p.args.m, p.args.n,
-                       p.args.k, p.args.status);
+  using S = ShapeOf<BN, Epi, X2>;
+  return launch_kernel(gemm_tc_kernel<BN, FP8, Epi, X2>, dim3(p.grid), dim3(S::kThreads), S::kSmemBytes, stream,
+                       p.map_a, p.map_a2, p.map_b, p.map_out, epi, p.args.m, p.args.n, p.args.k, p.args.status);
 }
 
-template <bool FP8, class Epi>
+template <bool FP8, bool X2, class Epi>
 cudaError_t launch_pair(const GemmPlan& p, const Epi& epi, cudaStream_t stream) {
-  using P = PairShape<Epi::kOutBytes, Epi::kWarps>;
-  return launch_kernel(gemm_pair_kernel<FP8, Epi>, dim3(p.grid), dim3(P::kThreads), P::kSmemBytes, stream, p.map_a,
-                       p.map_b, p.map_out, epi, p.args.m, p.args.n, p.args.k, p.args.status);
+  using P = PairShapeOf<Epi, X2>;
+  return launch_kernel(gemm_pair_kernel<FP8, Epi, X2>, dim3(p.grid), dim3(P::kThreads), P::kSmemBytes, stream,
+                       p.map_a, p.map_a2, p.map_b, p.map_out, epi, p.args.m, p.args.n, p.args.k, p.args.status);
 }
 
-template <bool FP8>
-cudaError_t launch_pair_epi(const GemmPlan& p, cudaStream_t stream) {
-  const GemmArgs& a = p.args;
+// The epilogue functor of `a` handed to `launch` (a single-CTA or CTA-pair launcher taking the
+// functor), for the epilogues that exist for these operand types.
+template <bool FP8, bool X2, class Launch>
+cudaError_t with_epilogue(const GemmArgs& a, Launch launch) {
   switch (a.epi) {
     case Epilogue::kBias:
-      return launch_pair<FP8>(p, EpiBiasBf16{a.bias, a.scale}, stream);
+      return launch(EpiBiasBf16{a.bias, a.scale});
     case Epilogue::kResidual:
-      return launch_pair<FP8>(p, EpiResidual{a.bias, a.scale}, stream);
+      return launch(EpiResidual{a.bias, a.scale});
     case Epilogue::kGeluBf16:
-      if constexpr (!FP8) return launch_pair<FP8>(p, EpiGelu<false>{a.bias, a.scale, a.inv_q}, stream);
-      break;
-    case Epilogue::kGeluE4m3:
-      if constexpr (FP8) return launch_pair<FP8>(p, EpiGelu<true>{a.bias, a.scale, a.inv_q}, stream);
+      if constexpr (!FP8) return launch(EpiGelu<false>{a.bias, a.scale, a.inv_q});
       break;
     case Epilogue::kGeluTanhBf16:
-      if constexpr (!FP8) return launch_pair<FP8>(p, EpiGeluTanh<false>{a.bias, a.scale, a.inv_q}, stream);
+      if constexpr (!FP8) return launch(EpiGeluTanh<false>{a.bias, a.scale, a.inv_q});
+      break;
+    case Epilogue::kGeluE4m3:
+      if constexpr (FP8 && !X2) return launch(EpiGelu<true>{a.bias, a.scale, a.inv_q});
       break;
     case Epilogue::kGeluTanhE4m3:
-      if constexpr (FP8) return launch_pair<FP8>(p, EpiGeluTanh<true>{a.bias, a.scale, a.inv_q}, stream);
+      if constexpr (FP8 && !X2) return launch(EpiGeluTanh<true>{a.bias, a.scale, a.inv_q});
       break;
-    default:
+    case Epilogue::kGeluE4m3x2:
+      if constexpr (X2) return launch(EpiGeluE4m3x2<false>{a.bias, a.scale, a.inv_q, a.n});
+      break;
+    case Epilogue::kGeluTanhE4m3x2:
+      if constexpr (X2) return launch(EpiGeluE4m3x2<true>{a.bias, a.scale, a.inv_q, a.n});
       break;
   }
   return cudaErrorInvalidValue;
 }
 
-template <bool FP8, class Epi>
+template <bool FP8, bool X2>
+cudaError_t launch_pair_epi(const GemmPlan& p, cudaStream_t stream) {
+  return with_epilogue<FP8, X2>(p.args, [&](const auto& epi) { return launch_pair<FP8, X2>(p, epi, stream); });
+}
+
+template <bool FP8, bool X2, class Epi>
 cudaError_t prepare_pair() {
-  return cudaFuncSetAttribute(gemm_pair_kernel<FP8, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              PairShape<Epi::kOutBytes, Epi::kWarps>::kSmemBytes);
+  return cudaFuncSetAttribute(gemm_pair_kernel<FP8, Epi, X2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              PairShapeOf<Epi, X2>::kSmemBytes);
 }
 
 // Smallest K planned on CTA pairs (N a multiple of 256): MRN_GEMM_PAIR=0 never, =2 from K = 512,
@@ -70,60 +83,43 @@ int pair_min_k() {
   return k;
 }
 
-template <int BN, bool FP8>
+template <int BN, bool FP8, bool X2>
 cudaError_t launch_bn(const GemmPlan& p, cudaStream_t stream) {
-  const GemmArgs& a = p.args;
-  switch (a.epi) {
-    case Epilogue::kBias:
-      return launch_one<BN, FP8>(p, EpiBiasBf16{a.bias, a.scale}, stream);
-    case Epilogue::kResidual:
-      return launch_one<BN, FP8>(p, EpiResidual{a.bias, a.scale}, stream);
-    case Epilogue::kGeluBf16:
-      if constexpr (!FP8) return launch_one<BN, FP8>(p, EpiGelu<false>{a.bias, a.scale, a.inv_q}, stream);
-      break;
-    case Epilogue::kGeluE4m3:
-      if constexpr (FP8) return launch_one<BN, FP8>(p, EpiGelu<true>{a.bias, a.scale, a.inv_q}, stream);
-      break;
-    case Epilogue::kGeluTanhBf16:
-      if constexpr (!FP8) return launch_one<BN, FP8>(p, EpiGeluTanh<false>{a.bias, a.scale, a.inv_q}, stream);
-      break;
-    case Epilogue::kGeluTanhE4m3:
-      if constexpr (FP8) return launch_one<BN, FP8>(p, EpiGeluTanh<true>{a.bias, a.scale, a.inv_q}, stream);
-      break;
-    default:
-      break;
-  }
-  return cudaErrorInvalidValue;
+  return with_epilogue<FP8, X2>(p.args, [&](const auto& epi) { return launch_one<BN, FP8, X2>(p, epi, stream); });
 }
 
-template <bool FP8>
-cudaError_t launch_fp8(const GemmPlan& p, cudaStream_t stream) {
+template <bool FP8, bool X2>
+cudaError_t launch_single(const GemmPlan& p, cudaStream_t stream) {
   switch (p.bn) {
-    case 256: return launch_bn<256, FP8>(p, stream);
-    case 192: return launch_bn<192, FP8>(p, stream);
-    case 128: return launch_bn<128, FP8>(p, stream);
-    case 64: return launch_bn<64, FP8>(p, stream);
+    case 256: return launch_bn<256, FP8, X2>(p, stream);
+    case 192: return launch_bn<192, FP8, X2>(p, stream);
+    case 128: return launch_bn<128, FP8, X2>(p, stream);
+    case 64: return launch_bn<64, FP8, X2>(p, stream);
   }
   return cudaErrorInvalidValue;
 }
 
-template <int BN, bool FP8, class Epi>
+template <int BN, bool FP8, bool X2, class Epi>
 cudaError_t prepare_one() {
-  return cudaFuncSetAttribute(gemm_tc_kernel<BN, FP8, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              ShapeOf<BN, Epi>::kSmemBytes);
+  return cudaFuncSetAttribute(gemm_tc_kernel<BN, FP8, Epi, X2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              ShapeOf<BN, Epi, X2>::kSmemBytes);
 }
 
 template <int BN>
 cudaError_t prepare_bn() {
   cudaError_t e;
-  if ((e = prepare_one<BN, false, EpiBiasBf16>()) != cudaSuccess) return e;
-  if ((e = prepare_one<BN, false, EpiResidual>()) != cudaSuccess) return e;
-  if ((e = prepare_one<BN, false, EpiGelu<false>>()) != cudaSuccess) return e;
-  if ((e = prepare_one<BN, false, EpiGeluTanh<false>>()) != cudaSuccess) return e;
-  if ((e = prepare_one<BN, true, EpiGeluTanh<true>>()) != cudaSuccess) return e;
-  if ((e = prepare_one<BN, true, EpiBiasBf16>()) != cudaSuccess) return e;
-  if ((e = prepare_one<BN, true, EpiResidual>()) != cudaSuccess) return e;
-  return prepare_one<BN, true, EpiGelu<true>>();
+  if ((e = prepare_one<BN, false, false, EpiBiasBf16>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, false, false, EpiResidual>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, false, false, EpiGelu<false>>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, false, false, EpiGeluTanh<false>>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, true, false, EpiGeluTanh<true>>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, true, false, EpiBiasBf16>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, true, false, EpiResidual>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, true, false, EpiGelu<true>>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, true, true, EpiBiasBf16>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, true, true, EpiResidual>()) != cudaSuccess) return e;
+  if ((e = prepare_one<BN, true, true, EpiGeluE4m3x2<false>>()) != cudaSuccess) return e;
+  return prepare_one<BN, true, true, EpiGeluE4m3x2<true>>();
 }
 
 }  // namespace
@@ -151,8 +147,17 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
     snprintf(err, 256, "gemm: K=%d rows are not a multiple of 16 bytes", args.k);
     return false;
   }
-  if ((args.epi == Epilogue::kGeluE4m3 || args.epi == Epilogue::kGeluTanhE4m3) && !args.fp8) {
-    snprintf(err, 256, "gemm: e4m3 GELU output is only planned for FP8 operands");
+  const bool x2_out = args.epi == Epilogue::kGeluE4m3x2 || args.epi == Epilogue::kGeluTanhE4m3x2;
+  if ((args.epi == Epilogue::kGeluE4m3 || args.epi == Epilogue::kGeluTanhE4m3) && (!args.fp8 || args.x2)) {
+    snprintf(err, 256, "gemm: e4m3 GELU output is only planned for one-term FP8 operands");
+    return false;
+  }
+  if (x2_out != args.x2 && args.epi != Epilogue::kBias && args.epi != Epilogue::kResidual) {
+    snprintf(err, 256, "gemm: two-term e4m3 GELU output is planned for two-term operands only");
+    return false;
+  }
+  if (args.x2 && (!args.fp8 || args.k % 16 != 0)) {
+    snprintf(err, 256, "gemm: two-term activations need e4m3 operands and K a multiple of 16 (K=%d)", args.k);
     return false;
   }
   if ((args.epi == Epilogue::kGeluBf16 || args.epi == Epilogue::kGeluTanhBf16) && args.fp8) {
@@ -170,7 +175,11 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
   // The memory-bound residual GEMMs with a short K (out-proj) run 128-column tiles with four
   // TMEM accumulators: the reduce-add stores drain behind three tiles of MMAs.
   if (!plan->pair && args.epi == Epilogue::kResidual && args.k < 1024 && args.n % 128 == 0) plan->bn = 128;
-  if (!make_kmajor_map(&plan->map_a, args.a, eb, args.m, args.k, kTileM) ||
+  // Two-term A: [M, 2K] with each row's K hi codes then its K lo codes, read through two maps.
+  const uint64_t a_row = args.x2 ? 2 * static_cast<uint64_t>(args.k) : 0;
+  if (!make_kmajor_map(&plan->map_a, args.a, eb, args.m, args.k, kTileM, a_row) ||
+      !make_kmajor_map(&plan->map_a2, args.x2 ? static_cast<const uint8_t*>(args.a) + args.k : args.a, eb, args.m,
+                       args.k, kTileM, a_row) ||
       !make_kmajor_map(&plan->map_b, args.b, eb, args.n, args.k, plan->pair ? 128 : plan->bn)) {
     snprintf(err, 256, "gemm: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", args.m, args.n, args.k);
     return false;
@@ -188,6 +197,12 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
       break;
     case Epilogue::kResidual:
       out_ok = make_store_map(&plan->map_out, args.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, args.m, args.n, args.ldo);
+      break;
+    case Epilogue::kGeluE4m3x2:
+    case Epilogue::kGeluTanhE4m3x2:
+      // [M, 2N]: the hi block of columns [n0 + c, +32) and the lo block N columns further on
+      out_ok = args.ldo >= 2 * args.n &&
+               make_store_map(&plan->map_out, args.out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, args.m, 2 * args.n, args.ldo);
       break;
   }
   if (!out_ok) {
@@ -207,14 +222,18 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
 
 cudaError_t gemm_prepare_device() {
   cudaError_t e;
-  if ((e = prepare_pair<false, EpiBiasBf16>()) != cudaSuccess) return e;
-  if ((e = prepare_pair<false, EpiResidual>()) != cudaSuccess) return e;
-  if ((e = prepare_pair<false, EpiGelu<false>>()) != cudaSuccess) return e;
-  if ((e = prepare_pair<false, EpiGeluTanh<false>>()) != cudaSuccess) return e;
-  if ((e = prepare_pair<true, EpiGeluTanh<true>>()) != cudaSuccess) return e;
-  if ((e = prepare_pair<true, EpiBiasBf16>()) != cudaSuccess) return e;
-  if ((e = prepare_pair<true, EpiResidual>()) != cudaSuccess) return e;
-  if ((e = prepare_pair<true, EpiGelu<true>>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<false, false, EpiBiasBf16>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<false, false, EpiResidual>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<false, false, EpiGelu<false>>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<false, false, EpiGeluTanh<false>>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<true, false, EpiGeluTanh<true>>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<true, false, EpiBiasBf16>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<true, false, EpiResidual>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<true, false, EpiGelu<true>>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<true, true, EpiBiasBf16>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<true, true, EpiResidual>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<true, true, EpiGeluE4m3x2<false>>()) != cudaSuccess) return e;
+  if ((e = prepare_pair<true, true, EpiGeluE4m3x2<true>>()) != cudaSuccess) return e;
   if ((e = prepare_bn<256>()) != cudaSuccess) return e;
   if ((e = prepare_bn<192>()) != cudaSuccess) return e;
   if ((e = prepare_bn<128>()) != cudaSuccess) return e;
@@ -231,8 +250,12 @@ cudaError_t gemm_test_hooks(unsigned long long wait_limit_ns, int no_loads, cuda
 #endif
 
 cudaError_t gemm_launch(const GemmPlan& plan, cudaStream_t stream) {
-  if (plan.pair) return plan.args.fp8 ? launch_pair_epi<true>(plan, stream) : launch_pair_epi<false>(plan, stream);
-  return plan.args.fp8 ? launch_fp8<true>(plan, stream) : launch_fp8<false>(plan, stream);
+  const GemmArgs& a = plan.args;
+  if (plan.pair)
+    return a.x2 ? launch_pair_epi<true, true>(plan, stream)
+                : a.fp8 ? launch_pair_epi<true, false>(plan, stream) : launch_pair_epi<false, false>(plan, stream);
+  return a.x2 ? launch_single<true, true>(plan, stream)
+              : a.fp8 ? launch_single<true, false>(plan, stream) : launch_single<false, false>(plan, stream);
 }
 
 }  // namespace mrn

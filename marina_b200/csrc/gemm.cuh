@@ -30,6 +30,7 @@
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 
+#include "e4m3x2.cuh"
 #include "ptx.cuh"
 
 namespace mrn {
@@ -41,11 +42,11 @@ constexpr int kEpiChunk = 32;        // columns per epilogue step
 constexpr int kMaxSmem = 232448;     // 227 KB per CTA
 
 // Shared memory of one (BN, epilogue) instantiation: the operand ring plus one 32 x 32 staging
-// block per epilogue warp.
-template <int BN, int EPI_WARPS, int OUT_BYTES>
+// block per epilogue warp. A_TERMS = 2 for two-term e4m3 activations (hi and lo A tiles per stage).
+template <int BN, int EPI_WARPS, int OUT_BYTES, int A_TERMS = 1>
 struct GemmShape {
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
-  static constexpr int kABytes = kTileM * kStageRowBytes;
+  static constexpr int kABytes = A_TERMS * kTileM * kStageRowBytes;
   static constexpr int kBBytes = BN * kStageRowBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiBufBytes = 32 * kEpiChunk * OUT_BYTES;
@@ -164,6 +165,7 @@ struct EpiBiasBf16 {
   static constexpr int kOutBytes = 2;
   static constexpr bool kReduce = false;
   static constexpr int kWarps = 8;
+  static constexpr int kTerms = 1;
   const float* bias;
   float scale;
   __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[4]) const {
@@ -193,6 +195,7 @@ struct EpiGelu {
   static constexpr int kOutBytes = E4M3 ? 1 : 2;
   static constexpr bool kReduce = false;
   static constexpr int kWarps = 16;
+  static constexpr int kTerms = 1;
   const float* bias;
   float scale;
   float inv_q;
@@ -255,6 +258,7 @@ struct EpiGeluTanh {
   static constexpr int kOutBytes = E4M3 ? 1 : 2;
   static constexpr bool kReduce = false;
   static constexpr int kWarps = 16;
+  static constexpr int kTerms = 1;
   const float* bias;
   float scale;
   float inv_q;
@@ -285,11 +289,49 @@ struct EpiGeluTanh {
   }
 };
 
+// out = GELU(acc * scale + bias) * inv_q as two-term e4m3 (hi = e4m3(v), lo = e4m3(v - hi)), the
+// erf form or (TANH) the tanh form, in f32: the row's 32 hi codes go to out[0..1] and its 32 lo codes
+// to out[2..3]. The kernel stores them as two 32-column blocks, the lo block lo_col columns to the
+// right of the hi block (an [M, 2N] output holding the hi codes, then the lo codes, of each row).
+template <bool TANH>
+struct EpiGeluE4m3x2 {
+  static constexpr int kOutBytes = 2;
+  static constexpr bool kReduce = false;
+  static constexpr int kWarps = 16;
+  static constexpr int kTerms = 2;
+  const float* bias;
+  float scale;
+  float inv_q;
+  int lo_col;
+  __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[4]) const {
+    float4 b[8];
+    load_bias32(bias, col, b);
+    const float2 s2 = make_float2(scale, scale), q2 = make_float2(inv_q, inv_q);
+    uint32_t* hi = reinterpret_cast<uint32_t*>(o);
+    uint32_t* lo = hi + 8;
+#pragma unroll
+    for (int c = 0; c < 32; c += 4) {
+      const float4 bb = b[c / 4];
+      float2 y0 = fma2(make_float2(v[c], v[c + 1]), s2, make_float2(bb.x, bb.y));
+      float2 y1 = fma2(make_float2(v[c + 2], v[c + 3]), s2, make_float2(bb.z, bb.w));
+      if constexpr (TANH) {
+        y0 = make_float2(gelu_tanh(y0.x), gelu_tanh(y0.y));
+        y1 = make_float2(gelu_tanh(y1.x), gelu_tanh(y1.y));
+      } else {
+        y0 = gelu2(y0);
+        y1 = gelu2(y1);
+      }
+      split_e4m3x4(mul2(y0, q2), mul2(y1, q2), hi[c / 4], lo[c / 4]);
+    }
+  }
+};
+
 // x += acc * scale + bias on the f16 residual stream, as a TMA reduce-add of the f16 values.
 struct EpiResidual {
   static constexpr int kOutBytes = 2;
   static constexpr bool kReduce = true;
   static constexpr int kWarps = 8;
+  static constexpr int kTerms = 1;
   const float* bias;
   float scale;
   __device__ __forceinline__ void pack(int col, const float (&v)[32], uint4 (&o)[4]) const {
@@ -306,11 +348,15 @@ struct EpiResidual {
 };
 
 // ---- the kernel ------------------------------------------------------------------------
-template <int BN, bool FP8, class Epi>
+// X2: two-term e4m3 A (e4m3 operands only): map_a reads the hi codes and map_a2 the lo codes of
+// each A tile; every MMA step runs on both into the same accumulator. Otherwise map_a2 is unused.
+template <int BN, bool FP8, class Epi, bool X2 = false>
 __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                   const __grid_constant__ CUtensorMap map_out, Epi epi, int M, int N, int K, int* status) {
-  using S = GemmShape<BN, Epi::kWarps, Epi::kOutBytes>;
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
+                   const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_out, Epi epi,
+                   int M, int N, int K, int* status) {
+  static_assert(FP8 || !X2, "two-term activations need e4m3 operands");
+  using S = GemmShape<BN, Epi::kWarps, Epi::kOutBytes, X2 ? 2 : 1>;
   constexpr int kStages = S::kStages;
   constexpr int kEpiWarps = Epi::kWarps;
   constexpr int kEpiBufBytes = S::kEpiBufBytes;
@@ -357,6 +403,7 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
     *abort = 0;
     fence_barrier_init();
     tma_prefetch_map(&map_a);
+    if constexpr (X2) tma_prefetch_map(&map_a2);
     tma_prefetch_map(&map_b);
     tma_prefetch_map(&map_out);
   }
@@ -392,6 +439,9 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
           }
           mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
           tma_load_2d(sm_a + stage * S::kABytes, &map_a, &full[stage], kb * kElemsPerStage, m0);
+          if constexpr (X2)
+            tma_load_2d(sm_a + stage * S::kABytes + kTileM * kStageRowBytes, &map_a2, &full[stage],
+                        kb * kElemsPerStage, m0);
           tma_load_2d(sm_b + stage * S::kBBytes, &map_b, &full[stage], kb * kElemsPerStage, n0);
           issued_mask |= 1u << stage;
           parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
@@ -436,10 +486,12 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
           for (int k = 0; k < kStageRowBytes / 32; ++k) {
             const uint64_t ad = desc_sw128(a_addr + 32u * k);
             const uint64_t bd = desc_sw128(b_addr + 32u * k);
-            if constexpr (FP8)
+            if constexpr (FP8) {
               mma_e4m3(d, ad, bd, kIdesc, (kb | k) != 0);
-            else
+              if constexpr (X2) mma_e4m3(d, desc_sw128(a_addr + kTileM * kStageRowBytes + 32u * k), bd, kIdesc, 1);
+            } else {
               mma_bf16(d, ad, bd, kIdesc, (kb | k) != 0);
+            }
           }
           issued = true;
           tc_commit(&empty[stage]);
@@ -499,17 +551,30 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
         buf = buf + 1 == S::kEpiBuffers ? 0 : buf + 1;
         if (lane == 0) bulk_wait_read<S::kEpiBuffers - 1>();
         __syncwarp();
+        if constexpr (Epi::kTerms == 2) {
+          // Two 32 x 32-byte blocks: the hi codes, then the lo codes.
 #pragma unroll
-        for (int j = 0; j < Epi::kOutBytes * 2; ++j)
-          *reinterpret_cast<uint4*>(sb + staged_offset<kRowBytes>(lane, j)) = out[j];
+          for (int j = 0; j < 2; ++j) {
+            *reinterpret_cast<uint4*>(sb + staged_offset<32>(lane, j)) = out[j];
+            *reinterpret_cast<uint4*>(sb + 1024 + staged_offset<32>(lane, j)) = out[2 + j];
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < Epi::kOutBytes * 2; ++j)
+            *reinterpret_cast<uint4*>(sb + staged_offset<kRowBytes>(lane, j)) = out[j];
+        }
         fence_async_shared();
         __syncwarp();
         if (lane == 0) {
           if (row0 < M) {
-            if constexpr (Epi::kReduce)
+            if constexpr (Epi::kReduce) {
               tma_reduce_add_2d(&map_out, sb, n0 + c, row0);
-            else
+            } else if constexpr (Epi::kTerms == 2) {
               tma_store_2d(&map_out, sb, n0 + c, row0);
+              tma_store_2d(&map_out, sb + 1024, epi.lo_col + n0 + c, row0);
+            } else {
+              tma_store_2d(&map_out, sb, n0 + c, row0);
+            }
           }
           bulk_commit();
         }
@@ -549,11 +614,11 @@ __global__ void __launch_bounds__(64 + 32 * Epi::kWarps, 1)
 // the leader's MMA commits to empty[s] and tmem_full[a] of both CTAs at once (multicast
 // commit); tmem_empty[a] lives in the leader and counts the epilogue warps of both CTAs (the
 // peer arrives remotely). Every wait is bounded as in the single-CTA kernel.
-template <int OUT_BYTES, int EPI_WARPS>
+template <int OUT_BYTES, int EPI_WARPS, int A_TERMS = 1>
 struct PairShape {
   static constexpr int kBN = 256;       // output columns per pair tile
   static constexpr int kBHalf = 128;    // B rows loaded by each CTA
-  static constexpr int kABytes = kTileM * kStageRowBytes;
+  static constexpr int kABytes = A_TERMS * kTileM * kStageRowBytes;
   static constexpr int kBBytes = kBHalf * kStageRowBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiBufBytes = 32 * kEpiChunk * OUT_BYTES;
@@ -569,11 +634,13 @@ struct PairShape {
   static constexpr int kThreads = 64 + 32 * EPI_WARPS;
 };
 
-template <bool FP8, class Epi>
+template <bool FP8, class Epi, bool X2 = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * Epi::kWarps, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                     const __grid_constant__ CUtensorMap map_out, Epi epi, int M, int N, int K, int* status) {
-  using S = PairShape<Epi::kOutBytes, Epi::kWarps>;
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
+                     const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_out, Epi epi,
+                     int M, int N, int K, int* status) {
+  static_assert(FP8 || !X2, "two-term activations need e4m3 operands");
+  using S = PairShape<Epi::kOutBytes, Epi::kWarps, X2 ? 2 : 1>;
   constexpr int BN = S::kBN;
   constexpr int kStages = S::kStages;
   constexpr int kEpiWarps = Epi::kWarps;
@@ -621,6 +688,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * Epi::kWarp
     *abort = 0;
     fence_barrier_init();
     tma_prefetch_map(&map_a);
+    if constexpr (X2) tma_prefetch_map(&map_a2);
     tma_prefetch_map(&map_b);
     tma_prefetch_map(&map_out);
   }
@@ -654,6 +722,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * Epi::kWarp
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
           const uint32_t bar = map_to_rank(smem_u32(&full[stage]), 0);
           tma_load_2d_pair(sm_a + stage * S::kABytes, &map_a, bar, kb * kElemsPerStage, m0);
+          if constexpr (X2)
+            tma_load_2d_pair(sm_a + stage * S::kABytes + kTileM * kStageRowBytes, &map_a2, bar, kb * kElemsPerStage,
+                             m0);
           tma_load_2d_pair(sm_b + stage * S::kBBytes, &map_b, bar, kb * kElemsPerStage, nb);
           issued_mask |= 1u << stage;
           parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
@@ -697,10 +768,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * Epi::kWarp
           for (int k = 0; k < kStageRowBytes / 32; ++k) {
             const uint64_t ad = desc_sw128(a_addr + 32u * k);
             const uint64_t bd = desc_sw128(b_addr + 32u * k);
-            if constexpr (FP8)
+            if constexpr (FP8) {
               mma_pair_e4m3(d, ad, bd, kIdesc, (kb | k) != 0);
-            else
+              if constexpr (X2)
+                mma_pair_e4m3(d, desc_sw128(a_addr + kTileM * kStageRowBytes + 32u * k), bd, kIdesc, 1);
+            } else {
               mma_pair_bf16(d, ad, bd, kIdesc, (kb | k) != 0);
+            }
           }
           issued = true;
           tc_commit_pair(&empty[stage], 0x3);
@@ -755,17 +829,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * Epi::kWarp
         buf = buf + 1 == S::kEpiBuffers ? 0 : buf + 1;
         if (lane == 0) bulk_wait_read<S::kEpiBuffers - 1>();
         __syncwarp();
+        if constexpr (Epi::kTerms == 2) {
+          // Two 32 x 32-byte blocks: the hi codes, then the lo codes.
 #pragma unroll
-        for (int j = 0; j < Epi::kOutBytes * 2; ++j)
-          *reinterpret_cast<uint4*>(sb + staged_offset<kRowBytes>(lane, j)) = out[j];
+          for (int j = 0; j < 2; ++j) {
+            *reinterpret_cast<uint4*>(sb + staged_offset<32>(lane, j)) = out[j];
+            *reinterpret_cast<uint4*>(sb + 1024 + staged_offset<32>(lane, j)) = out[2 + j];
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < Epi::kOutBytes * 2; ++j)
+            *reinterpret_cast<uint4*>(sb + staged_offset<kRowBytes>(lane, j)) = out[j];
+        }
         fence_async_shared();
         __syncwarp();
         if (lane == 0) {
           if (row0 < M) {
-            if constexpr (Epi::kReduce)
+            if constexpr (Epi::kReduce) {
               tma_reduce_add_2d(&map_out, sb, n0 + c, row0);
-            else
+            } else if constexpr (Epi::kTerms == 2) {
               tma_store_2d(&map_out, sb, n0 + c, row0);
+              tma_store_2d(&map_out, sb + 1024, epi.lo_col + n0 + c, row0);
+            } else {
+              tma_store_2d(&map_out, sb, n0 + c, row0);
+            }
           }
           bulk_commit();
         }

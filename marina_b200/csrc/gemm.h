@@ -15,6 +15,8 @@ enum class Epilogue : int {
   kResidual = 3,   // x f16 += acc*scale + bias                    (out-proj, FFN2)
   kGeluTanhBf16 = 5,  // kGeluBf16 with the tanh-form GELU             (FFN1 of Gelu::Tanh cards)
   kGeluTanhE4m3 = 6,  // kGeluE4m3 with the tanh-form GELU
+  kGeluE4m3x2 = 7,    // out [M, 2N] = two-term e4m3 of GELU(acc*scale + bias) * inv_q: hi codes, then lo codes
+  kGeluTanhE4m3x2 = 8,  // kGeluE4m3x2 with the tanh-form GELU
 };
 
 struct GemmArgs {
@@ -22,6 +24,7 @@ struct GemmArgs {
   const void* b = nullptr;  // weight [N, K], same type, row-major (PyTorch Linear layout)
   int m = 0, n = 0, k = 0;
   bool fp8 = false;          // operands are e4m3 (kind::f8f6f4) instead of bf16 (kind::f16)
+  bool x2 = false;           // (fp8) A is two-term e4m3 [M, 2K]: each row's K hi codes, then its K lo codes
   Epilogue epi = Epilogue::kBias;
   void* out = nullptr;       // bf16 / e4m3 output, or the f16 residual stream
   int ldo = 0;               // row stride of `out` in elements
@@ -33,6 +36,7 @@ struct GemmArgs {
 
 struct GemmPlan {
   CUtensorMap map_a;
+  CUtensorMap map_a2;  // x2: the lo codes of A (otherwise a copy of map_a)
   CUtensorMap map_b;
   CUtensorMap map_out;
   GemmArgs args;

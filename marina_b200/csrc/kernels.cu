@@ -24,7 +24,7 @@ template <int VPL, int VEC>
 __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedParams e, NormParams n, int rows, int d) {
   // gamma [d], beta [d], both times the output's 1/scale (1 for bf16 outputs)
   extern __shared__ __align__(16) float gb[];
-  const float oq = n.out_type == ActType::kE4m3 ? n.inv_q : 1.f;
+  const float oq = n.out_type != ActType::kBf16 ? n.inv_q : 1.f;
   for (int k = threadIdx.x; k < d; k += blockDim.x) {
     gb[k] = n.gamma[k] * oq;
     gb[d + k] = n.beta[k] * oq;
@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedParams e, NormParams
   r.store(e.x + static_cast<size_t>(row) * d, lane);
   if (!n.out) return;  // layer 0's QKV normalises x itself
   ln_apply(r, gb, gb + d, ln_stats(r, d, n.eps), lane);
-  const size_t off = static_cast<size_t>(row) * d * (n.out_type == ActType::kBf16 ? 2 : 1);
+  const size_t off = static_cast<size_t>(row) * d * act_row_bytes(n.out_type);
   r.store_act(static_cast<uint8_t*>(n.out) + off, n.out_type, 1.f, lane);
 }
 
@@ -80,17 +80,19 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedParams e, NormParams
 // flight (packed f16, VPL/2 registers each) while the current row is reduced. At 64 registers
 // a thread (d <= 512), four 256-thread blocks fit on an SM: 32 warps x 3 rows of reads
 // outstanding; wider rows get 128 registers and two blocks.
-template <int VPL>
+// (The two-term e4m3 store needs more registers at d = 512: three blocks of 80.)
+template <int VPL, ActType OUT>
 constexpr int ln_blocks_per_sm() {
-  return VPL > 16 ? 2 : 4;
+  return VPL > 16 ? 2 : (VPL == 16 && OUT == ActType::kE4m3x2) ? 3 : 4;
 }
 
-template <int VPL, int VEC>
-__global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel(const __half* __restrict__ x,
+// OUT (= n.out_type) is a template parameter so that each instantiation holds one store path.
+template <int VPL, int VEC, ActType OUT>
+__global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL, OUT>()) layernorm_kernel(const __half* __restrict__ x,
                                                                                  NormParams n, int rows, int d) {
   // gamma [d], beta [d], both times the output's 1/scale (1 for bf16 outputs)
   extern __shared__ __align__(16) float gb[];
-  const float oq = n.out_type == ActType::kE4m3 ? n.inv_q : 1.f;
+  const float oq = OUT != ActType::kBf16 ? n.inv_q : 1.f;
   for (int i = threadIdx.x; i < d; i += blockDim.x) {
     gb[i] = n.gamma[i] * oq;
     gb[d + i] = n.beta[i] * oq;
@@ -102,7 +104,7 @@ __global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel
   const int stride = gridDim.x * 8;
   int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
-  const size_t out_bytes = n.out_type == ActType::kBf16 ? 2 : 1;
+  constexpr size_t out_bytes = act_row_bytes(OUT);
   using Row = WarpRow<VPL, VEC>;
   using Raw = RawRow<VPL, VEC>;
   Raw r0, r1, r2;
@@ -116,7 +118,7 @@ __global__ void __launch_bounds__(256, ln_blocks_per_sm<VPL>()) layernorm_kernel
     r1 = r2;
     if (row + 3 * stride < rows) r2.load(x + static_cast<size_t>(row + 3 * stride) * d, lane);
     ln_apply(cur, gb, gb + d, ln_stats(cur, d, n.eps), lane);
-    cur.store_act(static_cast<uint8_t*>(n.out) + static_cast<size_t>(row) * d * out_bytes, n.out_type, 1.f, lane);
+    cur.template store_act<OUT>(static_cast<uint8_t*>(n.out) + static_cast<size_t>(row) * d * out_bytes, 1.f, lane);
     row += stride;
     if (row >= rows) break;
   }
@@ -303,10 +305,21 @@ struct NormLaunch {
     int dev = 0, sms = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    switch (n.out_type) {
+      case ActType::kBf16: return go<ActType::kBf16>(sms, d, x, n, rows, s);
+      case ActType::kE4m3: return go<ActType::kE4m3>(sms, d, x, n, rows, s);
+      case ActType::kE4m3x2: return go<ActType::kE4m3x2>(sms, d, x, n, rows, s);
+    }
+    return cudaErrorInvalidValue;
+  }
+
+  template <ActType OUT>
+  static cudaError_t go(int sms, int d, const __half* x, const NormParams& n, int rows, cudaStream_t s) {
     const int blocks_needed = (rows + 7) / 8;
-    const int resident = sms * ln_blocks_per_sm<VPL>();
+    const int resident = sms * ln_blocks_per_sm<VPL, OUT>();
     const int grid = blocks_needed < resident ? blocks_needed : resident;
-    return launch_kernel(layernorm_kernel<VPL, VEC>, dim3(grid), dim3(256), 2 * d * sizeof(float), s, x, n, rows, d);
+    return launch_kernel(layernorm_kernel<VPL, VEC, OUT>, dim3(grid), dim3(256), 2 * d * sizeof(float), s, x, n, rows,
+                         d);
   }
 };
 
@@ -346,7 +359,9 @@ struct LoadKernels {
     cudaFuncAttributes a;
     cudaError_t e;
     if ((e = cudaFuncGetAttributes(&a, embed_ln_kernel<VPL, VEC>)) != cudaSuccess) return e;
-    if ((e = cudaFuncGetAttributes(&a, layernorm_kernel<VPL, VEC>)) != cudaSuccess) return e;
+    if ((e = cudaFuncGetAttributes(&a, layernorm_kernel<VPL, VEC, ActType::kBf16>)) != cudaSuccess) return e;
+    if ((e = cudaFuncGetAttributes(&a, layernorm_kernel<VPL, VEC, ActType::kE4m3>)) != cudaSuccess) return e;
+    if ((e = cudaFuncGetAttributes(&a, layernorm_kernel<VPL, VEC, ActType::kE4m3x2>)) != cudaSuccess) return e;
     if ((e = cudaFuncGetAttributes(&a, heads_kernel<VPL, VEC>)) != cudaSuccess) return e;
     if ((e = cudaFuncGetAttributes(&a, value_out_kernel<VPL, VEC>)) != cudaSuccess) return e;
     return cudaFuncGetAttributes(&a, priors_to_half_kernel);

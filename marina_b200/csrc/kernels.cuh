@@ -10,8 +10,13 @@
 
 namespace mrn {
 
-// Activation storage of a GEMM operand produced by a kernel.
-enum class ActType : int { kBf16 = 0, kE4m3 = 1 };
+// Activation storage of a GEMM operand produced by a kernel. kE4m3x2 carries each value v (scaled
+// by the operand's inv_q) as two e4m3 terms, hi = e4m3(v) and lo = e4m3(v - hi): a row of width w
+// is 2w bytes, the w hi codes followed by the w lo codes.
+enum class ActType : int { kBf16 = 0, kE4m3 = 1, kE4m3x2 = 2 };
+
+// Bytes per element of a row of that storage.
+__host__ __device__ constexpr int act_row_bytes(ActType t) { return t == ActType::kE4m3 ? 1 : 2; }
 
 struct EmbedParams {
   const uint8_t* boards;     // [B, 66]

@@ -187,6 +187,17 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
   return d;
 }
 
+// d = a * b on two lanes.
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 pa, pb, pd;\n\t"
+      "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "mul.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 // ---- TMEM / tcgen05 ---------------------------------------------------------------------
 // Executed by one whole warp. The allocated TMEM address is written to `*slot`.
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {

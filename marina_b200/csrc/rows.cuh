@@ -9,6 +9,7 @@
 
 #include <type_traits>
 
+#include "e4m3x2.cuh"
 #include "kernels.cuh"
 #include "ptx.cuh"
 
@@ -94,10 +95,35 @@ struct WarpRow {
   }
 
   __device__ __forceinline__ void store_act(void* dst, ActType type, float inv_q, int lane) const {
+    if (type == ActType::kE4m3x2)
+      store_act<ActType::kE4m3x2>(dst, inv_q, lane);
+    else if (type == ActType::kBf16)
+      store_act<ActType::kBf16>(dst, inv_q, lane);
+    else
+      store_act<ActType::kE4m3>(dst, inv_q, lane);
+  }
+
+  // The same for an output type known at compile time.
+  template <ActType OUT>
+  __device__ __forceinline__ void store_act(void* dst, float inv_q, int lane) const {
 #pragma unroll
     for (int c = 0; c < kChunks; ++c) {
       const float* x = v + c * VEC;
-      if (type == ActType::kBf16) {
+      if constexpr (OUT == ActType::kE4m3x2) {
+        // hi codes at the element's column, lo codes d = 32 VPL bytes further on (inv_q applied).
+        uint8_t* o = static_cast<uint8_t*>(dst) + col(c, lane);
+        if constexpr (VEC == 4) {
+          uint32_t hi, lo;
+          split_e4m3x4(make_float2(x[0] * inv_q, x[1] * inv_q), make_float2(x[2] * inv_q, x[3] * inv_q), hi, lo);
+          *reinterpret_cast<uint32_t*>(o) = hi;
+          *reinterpret_cast<uint32_t*>(o + 32 * VPL) = lo;
+        } else {
+          uint16_t hi, lo;
+          split_e4m3x2(make_float2(x[0] * inv_q, x[1] * inv_q), hi, lo);
+          *reinterpret_cast<uint16_t*>(o) = hi;
+          *reinterpret_cast<uint16_t*>(o + 32 * VPL) = lo;
+        }
+      } else if constexpr (OUT == ActType::kBf16) {
         __nv_bfloat16* o = static_cast<__nv_bfloat16*>(dst) + col(c, lane);
         if constexpr (VEC == 4) {
           __nv_bfloat162 p[2] = {__floats2bfloat162_rn(x[0], x[1]), __floats2bfloat162_rn(x[2], x[3])};

@@ -108,7 +108,7 @@ int upload_weight(mrn_ctx* c, void** dst, const float* w, size_t count, float* s
   for (size_t i = 0; i < count; ++i)
     codes[i] = static_cast<uint8_t>(__nv_cvt_float_to_fp8(w[i] * inv, __NV_SATFINITE, __NV_E4M3));
   *scale = s;
-  if (c->precision == MRN_PRECISION_FP8) {
+  if (c->precision == MRN_PRECISION_FP8 || c->precision == MRN_PRECISION_FP8_X2) {
     int rc = dev_alloc(c, dst, count);
     if (rc) return rc;
     CK(cudaMemcpy(*dst, codes.data(), count, cudaMemcpyHostToDevice));
@@ -262,20 +262,20 @@ namespace {
 GemmArgs base_args(const mrn_ctx* c, int rows) {
   GemmArgs a;
   a.m = rows;
-  a.fp8 = c->precision == MRN_PRECISION_FP8;
+  a.fp8 = c->precision == MRN_PRECISION_FP8 || c->precision == MRN_PRECISION_FP8_X2;
+  a.x2 = c->precision == MRN_PRECISION_FP8_X2;
   a.status = c->status;
   return a;
 }
 
 float gemm_scale(const mrn_ctx* c, const DevLayer& D, int i) {
-  return c->precision == MRN_PRECISION_FP8 ? D.ws[i] * D.as[i] : D.ws[i];
+  return c->act != ActType::kBf16 ? D.ws[i] * D.as[i] : D.ws[i];
 }
 
 }  // namespace
 
 void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, GemmArgs (&g)[4]) {
   const int d = c->d, ff = c->dff;
-  const bool fp8 = c->precision == MRN_PRECISION_FP8;
   const DevLayer& D = c->dl[l];
   for (int i = 0; i < 4; ++i) g[i] = base_args(c, rows);
   // QKV: h -> qkv (bf16)
@@ -287,9 +287,10 @@ void layer_gemm_args(const mrn_ctx* c, int l, int rows, const LayerBuffers& b, G
   // FFN1: h -> ff = GELU(.), the card's form (the value head's GELU is always the erf one)
   const bool tanh_form = c->gelu == MRN_GELU_TANH;
   g[2].a = b.h, g[2].b = D.w_1, g[2].n = ff, g[2].k = d;
-  g[2].epi = fp8 ? (tanh_form ? Epilogue::kGeluTanhE4m3 : Epilogue::kGeluE4m3)
-                 : (tanh_form ? Epilogue::kGeluTanhBf16 : Epilogue::kGeluBf16);
-  g[2].out = b.ff, g[2].ldo = ff, g[2].bias = D.b_1, g[2].scale = gemm_scale(c, D, 2), g[2].inv_q = 1.f / D.as[3];
+  g[2].epi = c->act == ActType::kE4m3     ? (tanh_form ? Epilogue::kGeluTanhE4m3 : Epilogue::kGeluE4m3)
+             : c->act == ActType::kE4m3x2 ? (tanh_form ? Epilogue::kGeluTanhE4m3x2 : Epilogue::kGeluE4m3x2)
+                                          : (tanh_form ? Epilogue::kGeluTanhBf16 : Epilogue::kGeluBf16);
+  g[2].out = b.ff, g[2].ldo = c->act == ActType::kE4m3x2 ? 2 * ff : ff, g[2].bias = D.b_1, g[2].scale = gemm_scale(c, D, 2), g[2].inv_q = 1.f / D.as[3];
   // FFN2: ff -> x +=
   g[3].a = b.ff, g[3].b = D.w_2, g[3].n = d, g[3].k = ff, g[3].epi = Epilogue::kResidual, g[3].out = b.x;
   g[3].ldo = d, g[3].bias = D.b_2, g[3].scale = gemm_scale(c, D, 3);
@@ -511,7 +512,10 @@ void destroy(mrn_ctx* c) {
 }
 
 const char* precision_name(int p) {
-  return p == MRN_PRECISION_FP8 ? "fp8" : p == MRN_PRECISION_FP8_WEIGHTS ? "fp8-weights" : "bf16";
+  return p == MRN_PRECISION_FP8_X2    ? "fp8x2"
+         : p == MRN_PRECISION_FP8       ? "fp8"
+         : p == MRN_PRECISION_FP8_WEIGHTS ? "fp8-weights"
+                                          : "bf16";
 }
 
 }  // namespace
@@ -533,7 +537,7 @@ MRN_API int mrn_create(const mrn_arch* arch, const mrn_weights* weights, int dev
   };
   if (!arch || !weights) return bail(c->fail(MRN_ERR_ARGUMENT, "arch or weights is NULL"));
   if (max_batch < 1) return bail(c->fail(MRN_ERR_ARGUMENT, "max_batch %d < 1", max_batch));
-  if (precision < MRN_PRECISION_BF16 || precision > MRN_PRECISION_FP8)
+  if (precision < MRN_PRECISION_BF16 || precision > MRN_PRECISION_FP8_X2)
     return bail(c->fail(MRN_ERR_ARGUMENT, "unknown precision %d", precision));
   c->device = device, c->precision = precision, c->max_batch = max_batch, c->max_bucket = bucket_for(max_batch);
   c->d = arch->d_model, c->layers = arch->n_layers, c->heads = arch->n_heads, c->dff = arch->d_ff;
@@ -555,15 +559,16 @@ MRN_API int mrn_create(const mrn_arch* arch, const mrn_weights* weights, int dev
     return bail(c->fail(MRN_ERR_UNSUPPORTED, "%d tokens per position (the kernels are built for %d)", c->t, kTokens));
   if (c->gelu != MRN_GELU_ERF && c->gelu != MRN_GELU_TANH)
     return bail(c->fail(MRN_ERR_ARGUMENT, "gelu must be MRN_GELU_ERF or MRN_GELU_TANH, got %d", c->gelu));
-  if (precision == MRN_PRECISION_FP8) {
+  const bool static_act = precision == MRN_PRECISION_FP8 || precision == MRN_PRECISION_FP8_X2;
+  if (static_act) {
     if (!arch->fp8_amax)
-      return bail(c->fail(MRN_ERR_ARGUMENT, "FP8 needs the calibration (encoder.fp8.activation_amax); the card has none"));
+      return bail(c->fail(MRN_ERR_ARGUMENT, "e4m3 activations need the calibration (encoder.fp8.activation_amax); the card has none"));
     for (int i = 0; i < 4 * c->layers; ++i)
       if (!(arch->fp8_amax[i] > 0.f) || !isfinite(arch->fp8_amax[i]))
         return bail(c->fail(MRN_ERR_ARGUMENT, "fp8_amax[%d] must be positive and finite", i));
   }
-  c->act = precision == MRN_PRECISION_FP8 ? ActType::kE4m3 : ActType::kBf16;
-  c->act_bytes = precision == MRN_PRECISION_FP8 ? 1 : 2;
+  c->act = precision == MRN_PRECISION_FP8 ? ActType::kE4m3 : precision == MRN_PRECISION_FP8_X2 ? ActType::kE4m3x2 : ActType::kBf16;
+  c->act_bytes = mrn::act_row_bytes(c->act);
 
   int rc = check_weights(c, weights);
   if (rc) return bail(rc);
@@ -588,7 +593,7 @@ MRN_API int mrn_create(const mrn_arch* arch, const mrn_weights* weights, int dev
   mrn::static_scratch_setup(c);
 
   if ((rc = load_weights(c, weights))) return bail(rc);
-  if (precision == MRN_PRECISION_FP8)
+  if (static_act)
     for (int l = 0; l < c->layers; ++l)
       for (int i = 0; i < 4; ++i) c->dl[l].as[i] = arch->fp8_amax[4 * l + i] * kFp8Margin / kE4m3Max;
   if ((rc = alloc_buffers(c))) return bail(rc);

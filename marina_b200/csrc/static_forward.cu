@@ -11,8 +11,9 @@
 // The array holds kStaticScratchBytes (8 MiB) and is resident on every GPU on which a context has
 // been created, for the life of the process. How many positions fit depends on the network: one
 // position needs 65 rows of the residual stream (f16), the two GEMM inputs and the attention
-// output (bf16, or e4m3 for MRN_PRECISION_FP8), Q/K/V (bf16) and the FFN hidden layer, plus
-// two d-wide bf16 rows for the value head -- 0.67 MB for the `small` network in bf16 or fp8w
+// output (bf16; e4m3 for MRN_PRECISION_FP8; two e4m3 codes, as wide as bf16, for
+// MRN_PRECISION_FP8_X2), Q/K/V (bf16) and the FFN hidden layer, plus two d-wide bf16 rows for
+// the value head -- 0.67 MB for the `small` network in bf16 or fp8w
 // (12 positions; 17 in fp8) and 0.25 MB for `nano` (33 positions; 47 in fp8). Larger batches
 // are refused with MRN_ERR_BATCH_TOO_LARGE and a message naming the limit.
 //

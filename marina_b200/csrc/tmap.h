@@ -24,16 +24,18 @@ inline EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
-// A K-major operand [rows, k] (row stride = k elements) read in boxes of
+// A K-major operand [rows, k] (row stride = `row_elems` elements, k when 0) read in boxes of
 // `box_rows` rows x 128 bytes with 128-byte swizzling. `elem_bytes` is 2 (bf16) or 1 (e4m3).
 // Rows and columns outside the tensor read as zero. Returns false on failure.
 inline bool make_kmajor_map(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t k,
-                            uint32_t box_rows) {
+                            uint32_t box_rows, uint64_t row_elems = 0) {
   EncodeTiledFn fn = encode_tiled_fn();
   if (!fn) return false;
-  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (k * elem_bytes) % 16 != 0) return false;
+  if (row_elems == 0) row_elems = k;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (row_elems * elem_bytes) % 16 != 0 || row_elems < k)
+    return false;
   const cuuint64_t dims[2] = {k, rows};
-  const cuuint64_t strides[1] = {k * static_cast<uint64_t>(elem_bytes)};
+  const cuuint64_t strides[1] = {row_elems * static_cast<uint64_t>(elem_bytes)};
   const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / elem_bytes), box_rows};
   const cuuint32_t estrides[2] = {1, 1};
   const CUtensorMapDataType dt = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;

@@ -127,7 +127,8 @@ def c_arch(arch: Architecture):
 class B200Network(Network):
     """One GPU's evaluator: `CudaNetwork::new(arch, &weights, ordinal, max_batch, fp8)`
     (src/net/cuda/mod.rs:276-493) with `precision` one of "bf16", "fp8w" (e4m3 weights,
-    bf16 activations) or "fp8" (e4m3 weights and activations)."""
+    bf16 activations), "fp8" (e4m3 weights and activations) or "fp8x2" (e4m3 weights,
+    activations as two e4m3 terms each)."""
 
     def __init__(self, arch: Architecture, weights: Weights, device: int = 0, max_batch: int = 1024,
                  precision: str = "fp8w"):

@@ -15,8 +15,9 @@ T = 65
 
 
 def _attention(qkv, positions, d, heads, e4m3, inv_q):
+    """`e4m3`: 0 bf16 output, 1 e4m3 codes, 2 two-term e4m3 codes (rows of 2d bytes)."""
     lib = _lib.load_test()
-    out = torch.full((positions * T + 16, d), 0x55 if e4m3 else 7.0, device=qkv.device,
+    out = torch.full((positions * T + 16, 2 * d if e4m3 == 2 else d), 0x55 if e4m3 else 7.0, device=qkv.device,
                      dtype=torch.uint8 if e4m3 else torch.bfloat16)
     status = torch.zeros(1, dtype=torch.int32, device=qkv.device)
     rc = lib.mrn_test_attention(qkv.data_ptr(), out.data_ptr(), positions, d, heads, int(e4m3), inv_q,
@@ -44,7 +45,7 @@ def _reference(qkv, positions, d, heads):
 # small (8 x 64) and nano (6 x 32) heads; one position, a few, and more items than CTAs
 @pytest.mark.parametrize("d,heads", [(512, 8), (192, 6)])
 @pytest.mark.parametrize("positions", [1, 3, 37, 300])
-@pytest.mark.parametrize("e4m3", [False, True], ids=["bf16", "e4m3"])
+@pytest.mark.parametrize("e4m3", [0, 1, 2], ids=["bf16", "e4m3", "e4m3x2"])
 def test_attention_matches_torch(cuda, d, heads, positions, e4m3):
     g = torch.Generator(device="cuda").manual_seed(positions * 7 + d)
     # scores of a few units, so the softmax is far from uniform
@@ -53,7 +54,15 @@ def test_attention_matches_torch(cuda, d, heads, positions, e4m3):
     q = 0.02  # e4m3 codes up to 448 q: every output in range
     out = _attention(qkv, positions, d, heads, e4m3, 1.0 / q)
     rows = positions * T
-    if e4m3:
+    if e4m3 == 2:
+        # hi + lo: the residual after one e4m3 step, itself rounded to e4m3 (or to the subnormal
+        # step 2^-9), plus the bf16 rounding of P
+        codes = out[:rows].view(torch.float8_e4m3fn).float()
+        got = (codes[:, :d] + codes[:, d:]) * q
+        assert float(ref.abs().max()) < 448 * q
+        tol = ref.abs() * 2 ** -8 + q * 2 ** -10 + w * 2 ** -8 + 1e-4
+        assert bool((out[rows:] == 0x55).all())
+    elif e4m3:
         got = out[:rows].view(torch.float8_e4m3fn).float() * q
         assert float(ref.abs().max()) < 448 * q
         # one e4m3 step of the output, plus the bf16 rounding of P

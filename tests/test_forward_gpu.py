@@ -10,7 +10,7 @@ tolerance, src/net/verify.rs:62-66) below the oracle's best. Random-init policie
 to uniform and a few percent of positions have top-2 prior margins below 1e-4, which no
 implementation with a different summation order can resolve; the raw agreement is printed
 beside it. The >= 99% criterion applies to the bf16-activation precisions ("bf16", "fp8w", the
-default). e4m3 activations ("fp8", the reference's FP8 path) cannot meet it on these policies at
+default) and to two-term e4m3 activations ("fp8x2"). e4m3 activations ("fp8", the reference's FP8 path) cannot meet it on these policies at
 any scale granularity (tests/test_precision.py): their argmax floor is what the format itself
 reaches -- the float32 simulation of the same e4m3 rounding (torch_reference.forward_quantised,
 run on the GPU) on the same positions -- less FP8_SLACK, so the kernels are held to adding no
@@ -94,7 +94,7 @@ def nano_setup():
     return arch, w, boards, legal, counts
 
 
-@pytest.mark.parametrize("precision", ["bf16", "fp8w", "fp8"])
+@pytest.mark.parametrize("precision", ["bf16", "fp8w", "fp8", "fp8x2"])
 def test_nano_golden_config(nano_setup, precision):
     """Config 0 (nano, 64 positions): bf16 against the committed golden output, the FP8
     weight modes against the oracle run on the e4m3-quantised weights they compute with."""
@@ -122,7 +122,7 @@ def small_setup():
     return arch, w, boards, legal, counts, ref, ref_q
 
 
-@pytest.mark.parametrize("precision", ["fp8w", "fp8", "bf16"])
+@pytest.mark.parametrize("precision", ["fp8w", "fp8", "bf16", "fp8x2"])
 def test_small_config_batch_256(small_setup, precision):
     """Config 1: small net, e4m3 per-tensor weight quantisation, batch 256."""
     arch, w, boards, legal, counts, ref, ref_q = small_setup
@@ -165,7 +165,8 @@ def test_f16_priors_are_the_f32_priors_rounded(small_setup):
     net.close()
 
 
-@pytest.mark.parametrize("net,precision", [("nano", "bf16"), ("nano", "fp8w"), ("small", "fp8w"), ("small", "fp8")])
+@pytest.mark.parametrize("net,precision", [("nano", "bf16"), ("nano", "fp8w"), ("small", "fp8w"), ("small", "fp8"),
+                                           ("nano", "fp8x2"), ("small", "fp8x2")])
 def test_argmax_agreement_on_1024_positions(net, precision):
     """The argmax criterion on a sample large enough for a 1% bound to mean something."""
     arch = card(net)
@@ -177,7 +178,7 @@ def test_argmax_agreement_on_1024_positions(net, precision):
     check_against(priors, wdl, ref_p, ref_w, counts, precision, arch, w, boards, legal)
 
 
-@pytest.mark.parametrize("precision", ["bf16", "fp8w", "fp8"])
+@pytest.mark.parametrize("precision", ["bf16", "fp8w", "fp8", "fp8x2"])
 def test_tanh_gelu_card(precision):
     """A card trained with the tanh-form GELU ("gelu (tanh approximation)", src/net/model.rs:64-65):
     the encoder's FFN applies that form, the value head keeps erf (src/net/cpu.rs:130-133)."""
@@ -377,7 +378,7 @@ def _check_plans_against_oracle(outs, net, precision):
         check_against(out["priors"], out["wdl"], ref_p, ref_w, counts, precision, card(net), w, boards, legal)
 
 
-@pytest.mark.parametrize("net,precision", [("small", "fp8w"), ("small", "bf16"), ("small", "fp8")])
+@pytest.mark.parametrize("net,precision", [("small", "fp8w"), ("small", "bf16"), ("small", "fp8"), ("small", "fp8x2")])
 def test_cta_pair_plans(tmp_path, net, precision):
     """The GEMMs planned on CTA pairs from K = 512 (MRN_GEMM_PAIR=2: QKV and FFN1 as well), only from
     K = 1024 (the default below, FFN2) and never (MRN_GEMM_PAIR=0) agree with each other to f32
@@ -400,6 +401,7 @@ def test_cta_pair_plans(tmp_path, net, precision):
     ("nano", "bf16", {}),
     ("small", "fp8w", {}),
     ("small", "fp8w", {"MRN_GEMM_PAIR": "2"}),
+    ("small", "fp8x2", {"MRN_GEMM_PAIR": "2"}),
 ])
 def test_programmatic_launch_changes_no_result(tmp_path, net, precision, extra):
     """Kernels launched with programmatic dependent launch (MRN_PDL=1: each kernel's launch and

@@ -14,6 +14,7 @@ pytestmark = pytest.mark.gpu
 
 EPI_BIAS, EPI_GELU_BF16, EPI_GELU_E4M3, EPI_RESIDUAL = 0, 1, 2, 3
 EPI_GELU_TANH_BF16, EPI_GELU_TANH_E4M3 = 5, 6
+EPI_GELU_E4M3X2, EPI_GELU_TANH_E4M3X2 = 7, 8
 
 # (M, N, K): QKV, out-proj, FFN1, FFN2 of both nets; M = positions x 65.
 SHAPES = [
@@ -59,6 +60,67 @@ def _operands(m, n, k, fp8, seed):
         return a8.view(torch.uint8), b8.view(torch.uint8), a8.float(), b8.float(), bias
     ab, bb = a.to(torch.bfloat16), b.to(torch.bfloat16)
     return ab, bb, ab.float(), bb.float(), bias
+
+
+def _x2_split(v):
+    """Two-term e4m3 of `v` (already in code units): hi = e4m3(v), lo = e4m3(v - hi)."""
+    hi = v.clamp(-448, 448).to(torch.float8_e4m3fn)
+    lo = (v - hi.float()).to(torch.float8_e4m3fn)
+    return hi, lo
+
+
+def _x2_operands(m, n, k, seed):
+    """A as two-term e4m3 [m, 2k] (each row's hi codes, then its lo codes), B as e4m3; the float
+    values are hi + lo and the B codes."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    a = torch.randn(m, k, device="cuda", generator=g) * (448.0 / 6.0)
+    b = torch.randn(n, k, device="cuda", generator=g) * 0.05
+    bias = torch.randn(n, device="cuda", generator=g) * 0.1
+    hi, lo = _x2_split(a)
+    a2 = torch.cat([hi.view(torch.uint8), lo.view(torch.uint8)], 1).contiguous()
+    b8 = (b * 8).to(torch.float8_e4m3fn)
+    return a2, b8.view(torch.uint8), hi.float() + lo.float(), b8.float(), hi.float(), bias
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_two_term_operands(cuda, m, n, k):
+    """Two-term e4m3 A: the product is (hi + lo) . b, held to the bf16 output's rounding, which is
+    far below what dropping the lo term would cost (about 2^-5 of each product)."""
+    a2, b, af, bf, hif, bias = _x2_operands(m, n, k, seed=m + 2 * n + k)
+    scale = 2.0 ** -12
+    out = torch.full((m, n), float("nan"), device=cuda, dtype=torch.bfloat16)
+    _run(2, EPI_BIAS, a2, b, bias, out, n, m, n, k, scale=scale)
+    ref = (af @ bf.T) * scale + bias
+    tol = ref.abs() * 2 ** -8 + 1e-4 * float(ref.abs().max())
+    _within(out.float(), ref, tol, "two-term bias")
+    # the tolerance has the power to see a dropped lo term
+    hi_only = (hif @ bf.T) * scale + bias
+    assert not bool(((hi_only - ref).abs() <= tol).all())
+    x0 = torch.randn(m, n, device=cuda).half()
+    x = x0.clone()
+    _run(2, EPI_RESIDUAL, a2, b, bias, x, n, m, n, k, scale=scale)
+    delta = (af @ bf.T) * scale + bias
+    ref = x0.float() + delta
+    _within(x.float(), ref, (ref.abs() + delta.abs()) * 2 ** -10 + 2 ** -14, "two-term residual")
+
+
+@pytest.mark.parametrize("m,n,k", [s for s in SHAPES if s[1] in (768, 2048, 256)])
+@pytest.mark.parametrize("epi", [EPI_GELU_E4M3X2, EPI_GELU_TANH_E4M3X2], ids=["erf", "tanh"])
+def test_gelu_two_term_epilogue(cuda, m, n, k, epi):
+    """GELU into two-term e4m3 [m, 2n] (hi codes in columns [0, n), lo codes in [n, 2n)), from
+    two-term operands, as FFN1 of the fp8x2 precision writes FFN2's input."""
+    a2, b, af, bf, _, bias = _x2_operands(m, n, k, seed=19 + epi)
+    scale, q = 2.0 ** -12, 0.01  # output value = (hi + lo) * q
+    out = torch.full((m, 2 * n + 32), 0x55, device=cuda, dtype=torch.uint8)
+    _run(2, epi, a2, b, bias, out, 2 * n + 32, m, n, k, scale=scale, inv_q=1.0 / q)
+    approx = "tanh" if epi == EPI_GELU_TANH_E4M3X2 else "none"
+    ref = torch.nn.functional.gelu((af @ bf.T) * scale + bias, approximate=approx)
+    assert float(ref.abs().max()) < 448 * q
+    codes = out[:, :2 * n].view(torch.float8_e4m3fn).float()
+    got = (codes[:, :n] + codes[:, n:]) * q
+    # the residual after one e4m3 step rounded to e4m3 (or to the subnormal step 2^-9)
+    _within(got, ref, ref.abs() * 2 ** -8 + q * 2 ** -10 + 1e-5, "two-term GELU")
+    assert bool((out[:, 2 * n:] == 0x55).all())
 
 
 @pytest.mark.parametrize("fp8", [False, True], ids=["bf16", "e4m3"])
@@ -156,16 +218,20 @@ def _norm_inputs(m, d, seed):
     return x, gamma, beta
 
 
-@pytest.mark.parametrize("e4m3", [False, True], ids=["bf16", "e4m3"])
+@pytest.mark.parametrize("e4m3", [0, 1, 2], ids=["bf16", "e4m3", "e4m3x2"])
 @pytest.mark.parametrize("m,d", [(65 * 7, 512), (65 * 3, 192), (1, 512), (65 * 64, 512), (130, 1024)])
 def test_layernorm_kernel(cuda, e4m3, m, d):
     """The LayerNorm kernel against torch fp32 LayerNorm of the same f16 rows."""
     x, gamma, beta = _norm_inputs(m, d, seed=m + d)
     q, eps = 0.02, 1e-5
-    out = torch.zeros((m, d), device=cuda, dtype=torch.uint8 if e4m3 else torch.bfloat16)
+    out = torch.zeros((m, 2 * d if e4m3 == 2 else d), device=cuda, dtype=torch.uint8 if e4m3 else torch.bfloat16)
     _layernorm(x, gamma, beta, eps, e4m3, 1.0 / q, out)
     ref = torch.nn.functional.layer_norm(x.float(), (d,), gamma, beta, eps)
-    if e4m3:
+    if e4m3 == 2:
+        codes = out.view(torch.float8_e4m3fn).float()
+        got = (codes[:, :d] + codes[:, d:]) * q
+        _within(got, ref, ref.abs() * 2 ** -8 + q * 2 ** -10 + 1e-5, "layernorm two-term e4m3")
+    elif e4m3:
         got = out.view(torch.float8_e4m3fn).float() * q
         _within(got, ref, ref.abs() * 0.0625 + q * 2 ** -6 + 1e-5, "layernorm e4m3")
     else:

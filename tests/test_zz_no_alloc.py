@@ -31,7 +31,7 @@ def _card(name):
 
 
 @pytest.mark.parametrize("net,precision,n,limit", [("nano", "bf16", 8, 33), ("small", "fp8", 17, 17),
-                                                   ("small", "fp8w", 12, 12)])
+                                                   ("small", "fp8w", 12, 12), ("small", "fp8x2", 12, 12)])
 def test_static_scratch_forward_matches_the_allocating_entry_point(net, precision, n, limit):
     if not torch.cuda.is_available():
         pytest.fail("GPU test run without a CUDA device")

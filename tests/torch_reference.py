@@ -74,11 +74,18 @@ def quantise(x: torch.Tensor, mode: str | None, amax: float) -> torch.Tensor:
     the reference's FP8 path (src/net/cuda/mod.rs:83-90, 454-466); "row" = e4m3 with a dynamic
     scale per row (row amax / 448); "mx32" = e4m3 with one power-of-two scale per 32 consecutive
     elements of the row (the OCP MX block scaling B200's block-scaled MMA reads); "nv16" = e4m3
-    with an exact (float32) scale per 16 elements (block amax / 448)."""
+    with an exact (float32) scale per 16 elements (block amax / 448); "x2" = two e4m3 terms with the
+    static per-tensor scale s, hi = e4m3(x / s) and lo = e4m3(x / s - hi), taken as (hi + lo) * s
+    (the fp8x2 precision)."""
     if mode is None:
         return x
     if mode == "bf16":
         return x.to(torch.bfloat16).to(torch.float32)
+    if mode == "x2":
+        s = amax * 1.25 / 448.0
+        v = x / s
+        hi = e4m3_round(v)
+        return (hi + (v - hi).to(torch.float8_e4m3fn).to(torch.float32)) * s
     if mode == "tensor":
         s = amax * 1.25 / 448.0
         return e4m3_round(x / s) * s
