@@ -235,7 +235,7 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
+        sm, watts, mx, reasons = [], [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.lines:
             f = [x.strip() for x in line.split(",")]
@@ -246,11 +246,15 @@ class ClockSampler:
                 mx = float(f[2])
             except ValueError:
                 continue
+            try:
+                watts.append(float(f[3]))
+            except ValueError:
+                pass
             for name, v in zip(names, f[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(name)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "power_w": float(np.median(watts)) if watts else None, "samples": len(sm)}
 
 
 def measure_fp8_peak(dev, seconds: float = 1.5) -> float | None:
