@@ -62,6 +62,9 @@ def parse_args():
     ap.add_argument("--nodes", type=int, default=100_000)
     ap.add_argument("--positions", type=int, default=1 << 20)
     ap.add_argument("--chunk", type=int, default=8192)
+    ap.add_argument("--ctx-per-gpu", type=int, default=1,
+                    help="wholebox: evaluator contexts per GPU (each takes a shard of every chunk; two overlap "
+                         "one shard's copies and launches with the other's kernels)")
     ap.add_argument("--scan", action="store_true", help="puct / wholebox: measure at 1, 2, 4, ... up to --gpus GPUs")
     return ap.parse_args()
 
@@ -588,26 +591,34 @@ def run_wholebox(args):
     flops = flops_per_eval(arch)
     cpu = cpu_baseline(args, arch, w, args.cpu_seconds) if not args.no_cpu_baseline else None
     for n_gpus in gpu_counts(args):
-        group = GroupNetwork(arch, w, list(range(n_gpus)), max_batch=chunk, precision=args.precision)
+        devices = [g for g in range(n_gpus) for _ in range(args.ctx_per_gpu)]
+        group = GroupNetwork(arch, w, devices, max_batch=chunk, precision=args.precision)
         group.evaluate_packed(hb[:chunk], hl[:chunk], hp[:chunk], hw[:chunk])  # graphs, clocks
+        # One call per chunk (each ends when its slowest shard does), then the whole job in one
+        # call, which the library runs as the same chunks with no barrier between them.
+        t0 = time.perf_counter()
+        for a in range(0, args.positions, chunk):
+            b = min(a + chunk, args.positions)
+            group.evaluate_packed(hb[a:b], hl[a:b], hp[a:b], hw[a:b])
+        per_chunk_value = args.positions / (time.perf_counter() - t0)
         with ClockSampler(0) as clocks:
             t0 = time.perf_counter()
-            for a in range(0, args.positions, chunk):
-                b = min(a + chunk, args.positions)
-                group.evaluate_packed(hb[a:b], hl[a:b], hp[a:b], hw[a:b])
+            group.evaluate_packed(hb, hl, hp, hw)
             el = time.perf_counter() - t0
         value = args.positions / el
         tensor_frac = value * flops / (n_gpus * gemm_peak)
         hbm_frac = value * bytes_per_eval / (n_gpus * hbm)
         line = {"mode": "wholebox", "net": args.net, "precision": args.precision, "gpus": n_gpus,
-                "positions": args.positions, "chunk": chunk, "seconds": el, "evals_per_s": value,
+                "positions": args.positions, "chunk": chunk, "contexts_per_gpu": args.ctx_per_gpu,
+                "seconds": el, "evals_per_s": value, "evals_per_s_one_call_per_chunk": per_chunk_value,
                 "roofline": {"bound": "tensor" if args.net == "small" else "hbm",
                              "frac": tensor_frac if args.net == "small" else hbm_frac,
                              "tensor_frac": tensor_frac, "hbm_frac": hbm_frac,
                              "flops_per_eval": flops, "layer_boundary_bytes_per_eval": bytes_per_eval,
                              "peaks": {"gemm_tflops": gemm_peak / 1e12, "hbm_gbs": hbm / 1e9,
                                        "source": "MEASURED_PEAKS.json (bf16 sustained; x2 for e4m3)"}},
-                "path": "mrn_group_evaluate per chunk (pinned host buffers; per GPU: H2D + graph + D2H)",
+                "path": "one mrn_group_evaluate over all positions: chunks of --chunk, shards taken by the "
+                        "device threads as they free up (pinned host buffers; per shard: H2D + graph + D2H)",
                 "input_generation_s": gen_s, "clocks_gpu0": clocks.summary(), "describe": group.describe()}
         if cpu:
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}

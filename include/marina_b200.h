@@ -218,7 +218,11 @@ MRN_API int mrn_group_create(const mrn_arch* arch, const mrn_weights* weights, c
 /* `mrn_evaluate` over the group: the batch is cut into n_devices contiguous shards (sizes differ by
  * at most one position), evaluated at the same time, one per device, and written into `priors` /
  * `wdl` at the shard's offset, so the outputs are in input order. No data moves between GPUs.
- * On failure the message names the device and the shard's positions. */
+ * A batch larger than the group's max_batch is evaluated as consecutive max_batch chunks cut the
+ * same way; after the first chunk each device thread takes the next shard as soon as it is free,
+ * without waiting for the others between chunks. On failure the message names the device and the
+ * shard's positions, and shards not yet started are skipped (outputs of the batch are then
+ * undefined). */
 MRN_API int mrn_group_evaluate(mrn_group* group, int n, const uint8_t* boards, const int32_t* legal, float* priors,
                                float* wdl);
 MRN_API int mrn_group_size(mrn_group* group);

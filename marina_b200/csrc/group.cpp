@@ -5,11 +5,18 @@
 // Positions are independent (the forward pass has no cross-position term), so no data moves
 // between GPUs and no collective is involved.
 //
+// A batch larger than max_batch is a sequence of max_batch chunks, each cut the same way. The
+// first chunk's shards go one to each device thread; every later shard is taken from a shared
+// counter by whichever thread is free, so no thread waits for the others between chunks (a GPU
+// that finishes early starts on the next chunk, and two contexts on one GPU drift apart, one
+// copying or launching while the other's kernels run).
+//
 // The reference has no multi-GPU path (its backend is built on ordinal 0, src/net/mod.rs:171-192);
 // this is the sharding wrapper around `Network` that the drop-in needs for a whole box.
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <condition_variable>
 #include <mutex>
 #include <string>
@@ -22,9 +29,10 @@ namespace {
 
 thread_local std::string g_group_create_error;
 
-struct Shard {
-  int begin = 0, count = 0;
+// A failed shard: its status, the thread (context) that ran it and its positions.
+struct Failure {
   int rc = MRN_OK;
+  int thread = 0, begin = 0, count = 0;
 };
 
 }  // namespace
@@ -46,7 +54,10 @@ struct mrn_group {
   const int32_t* legal = nullptr;
   float* priors = nullptr;
   float* wdl = nullptr;
-  std::vector<Shard> shards;
+  int max_batch = 0;
+  int pieces = 0;                  // shards of the whole call: chunks x contexts
+  std::atomic<int> next_piece{0};  // the next shard to take after each thread's first
+  Failure failure;                 // the first failure (under `mu`)
 
   std::string describe;
   std::string last_error;
@@ -61,13 +72,36 @@ struct mrn_group {
     return code;
   }
 
+  // Positions [begin, begin + count) of shard `piece`: chunk piece / k, its (piece % k)-th
+  // contiguous part (part sizes differ by at most one position).
+  void piece_range(int piece, int* begin, int* count) const {
+    const int k = static_cast<int>(ctx.size());
+    const int chunk = piece / k, part = piece % k;
+    const int c0 = chunk * max_batch, cn = (n - c0 < max_batch ? n - c0 : max_batch);
+    const int q = cn / k, r = cn % k;
+    *begin = c0 + part * q + (part < r ? part : r);
+    *count = q + (part < r ? 1 : 0);
+  }
+
+  bool evaluate_piece(int i, int piece) {
+    int begin = 0, count = 0;
+    piece_range(piece, &begin, &count);
+    if (count == 0) return true;
+    const size_t b = static_cast<size_t>(begin);
+    const int rc = mrn_evaluate(ctx[i], count, boards + b * MRN_BOARD_BYTES, legal + b * MRN_MAX_LEGAL,
+                                priors + b * MRN_MAX_LEGAL, wdl + b * MRN_WDL);
+    if (rc == MRN_OK) return true;
+    std::lock_guard<std::mutex> lock(mu);
+    if (failure.rc == MRN_OK) failure = Failure{rc, i, begin, count};
+    next_piece.store(pieces);  // hand out nothing more
+    return false;
+  }
+
+  // Thread i's part of a call: shard i of the first chunk, then shards from the shared counter.
   void run_shard(int i) {
-    Shard& s = shards[i];
-    s.rc = MRN_OK;
-    if (s.count == 0) return;
-    const size_t b = static_cast<size_t>(s.begin);
-    s.rc = mrn_evaluate(ctx[i], s.count, boards + b * MRN_BOARD_BYTES, legal + b * MRN_MAX_LEGAL,
-                        priors + b * MRN_MAX_LEGAL, wdl + b * MRN_WDL);
+    if (i < pieces && !evaluate_piece(i, i)) return;
+    for (int p = next_piece.fetch_add(1); p < pieces; p = next_piece.fetch_add(1))
+      if (!evaluate_piece(i, p)) return;
   }
 
   void worker(int i) {
@@ -131,7 +165,7 @@ MRN_API int mrn_group_create(const mrn_arch* arch, const mrn_weights* weights, c
     g->ctx.push_back(c);
     g->devices.push_back(devices[i]);
   }
-  g->shards.resize(n_devices);
+  g->max_batch = max_batch;
   for (int i = 1; i < n_devices; ++i) g->workers.emplace_back(&mrn_group::worker, g, i);
   g->describe = std::string(mrn_describe(g->ctx[0])) + " x " + std::to_string(n_devices) + " devices (";
   for (int i = 0; i < n_devices; ++i) g->describe += (i ? "," : "") + std::to_string(devices[i]);
@@ -151,15 +185,13 @@ MRN_API int mrn_group_evaluate(mrn_group* g, int n, const uint8_t* boards, const
   if (n < 0) return g->fail(MRN_ERR_ARGUMENT, "n = %d", n);
   if (n == 0) return MRN_OK;
   if (!boards || !legal || !priors || !wdl) return g->fail(MRN_ERR_ARGUMENT, "NULL buffer");
-  // Contiguous shards whose sizes differ by at most one position.
-  for (int i = 0, begin = 0; i < k; ++i) {
-    const int count = n / k + (i < n % k ? 1 : 0);
-    g->shards[i].begin = begin, g->shards[i].count = count;
-    begin += count;
-  }
+  const int chunks = (n + g->max_batch - 1) / g->max_batch;
   {
     std::lock_guard<std::mutex> lock(g->mu);
     g->n = n, g->boards = boards, g->legal = legal, g->priors = priors, g->wdl = wdl;
+    g->pieces = chunks * k;
+    g->next_piece.store(k);
+    g->failure = Failure{};
     g->pending = k - 1;
     ++g->generation;
   }
@@ -169,12 +201,10 @@ MRN_API int mrn_group_evaluate(mrn_group* g, int n, const uint8_t* boards, const
     std::unique_lock<std::mutex> lock(g->mu);
     g->done.wait(lock, [&] { return g->pending == 0; });
   }
-  for (int i = 0; i < k; ++i) {
-    const Shard& s = g->shards[i];
-    if (s.rc)
-      return g->fail(s.rc, "device %d, positions [%d, %d): %s", g->devices[i], s.begin, s.begin + s.count,
-                     mrn_last_error(g->ctx[i]));
-  }
+  const Failure f = g->failure;
+  if (f.rc)
+    return g->fail(f.rc, "device %d, positions [%d, %d): %s", g->devices[f.thread], f.begin, f.begin + f.count,
+                   mrn_last_error(g->ctx[f.thread]));
   return MRN_OK;
 }
 

@@ -263,7 +263,9 @@ class GroupNetwork(Network):
     """`Network` over one weight replica per listed device through `mrn_group_create` /
     `mrn_group_evaluate`: every batch is cut into contiguous shards (sizes differing by at most
     one position), evaluated at the same time by the library's per-device threads and written
-    into the outputs in input order. A failing shard raises `NetworkError` naming its device."""
+    into the outputs in input order. A batch larger than `max_batch` runs as consecutive
+    `max_batch` chunks whose shards the threads take as they become free. A failing shard raises
+    `NetworkError` naming its device and positions."""
 
     def __init__(self, arch: Architecture, weights: Weights, devices: Sequence[int], max_batch: int = 1024,
                  precision: str = "fp8w"):

@@ -68,7 +68,8 @@ def test_passes_on_two_streams_and_the_host_path_are_ordered(cuda, nano):
 def test_group_matches_one_context(cuda, nano, n_devices):
     """A group of contexts (all on device 0 here: a device may be listed more than once) gives each
     position the answer one context gives it, in input order, for batches that split evenly, unevenly
-    and into fewer positions than devices; and refuses a batch larger than its max_batch."""
+    and into fewer positions than devices, and for batches of several max_batch chunks (shards taken
+    from the shared queue); a failing shard is reported with its device and positions."""
     arch, w, boards, legal, counts = nano
     one = B200Network(arch, w, device=0, max_batch=96, precision="bf16")
     group = GroupNetwork(arch, w, [0] * n_devices, max_batch=96, precision="bf16")
@@ -81,9 +82,22 @@ def test_group_matches_one_context(cuda, nano, n_devices):
     leaves = [(boards[i], legal[i, :counts[i]].tolist()) for i in range(10)]
     evs = group.evaluate(leaves)
     assert [len(e.priors) for e in evs] == list(counts[:10])
-    with pytest.raises(NetworkError) as e:  # 97 positions: the first shard exceeds its context's max_batch
-        group.evaluate_packed(np.concatenate([boards, boards[:1]]), np.concatenate([legal, legal[:1]]))
-    assert e.value.code == 3 and "device 0" in str(e.value)
+    big_b, big_l = np.concatenate([boards] * 4), np.concatenate([legal] * 4)
+    for n in (97, 250, 384):  # 2, 3 and 4 chunks of max_batch, the last ragged or full
+        pg, wg = group.evaluate_packed(big_b[:n], big_l[:n])
+        for a in range(0, n, 96):
+            p1, w1 = one.evaluate_packed(big_b[a:min(n, a + 96)], big_l[a:min(n, a + 96)])
+            assert np.abs(p1 - pg[a:a + len(p1)]).max() <= 1e-6 and np.abs(w1 - wg[a:a + len(w1)]).max() <= 1e-6, n
+    bad_l = big_l[:250].copy()
+    bad_l[150, 0] = 5000  # an action index outside [0, 4672) in the second chunk
+    with pytest.raises(NetworkError) as e:
+        group.evaluate_packed(big_b[:250], bad_l)
+    assert e.value.code == 7 and "device 0" in str(e.value), str(e.value)
+    lo, hi = (int(x) for x in str(e.value).split("positions [")[1].split(")")[0].split(", "))
+    assert lo <= 150 < hi, str(e.value)
+    pg, wg = group.evaluate_packed(big_b[:96], big_l[:96])  # the group serves the next call
+    p1, w1 = one.evaluate_packed(big_b[:96], big_l[:96])
+    assert np.abs(p1 - pg).max() <= 1e-6 and np.abs(w1 - wg).max() <= 1e-6
     group.close()
     one.close()
 
