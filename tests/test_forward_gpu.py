@@ -200,6 +200,44 @@ def test_tanh_gelu_card(precision):
     assert float(np.abs(p_erf - priors).max()) > 1e-5
 
 
+@pytest.fixture(scope="module")
+def width_cases():
+    """Per supported (d_model, heads, d_ff) of a 2-layer network: the card with an FP8 calibration
+    from its own float32 forward, the weights, 128 positions and the oracle's output on the fp32
+    and on the e4m3-quantised weights (computed once per width, shared by the precisions)."""
+    from tests import torch_reference as tr
+
+    cache = {}
+
+    def get(d, heads, ff):
+        if (d, heads, ff) not in cache:
+            arch = model.Architecture(d, 2, heads, ff, 1e-5, model.GELU_ERF, None, 65, 1, 0, {})
+            w = weights.random_init(arch, seed=d + heads)
+            boards, legal, counts, _ = chess.random_positions(d, 128, 0, 80)
+            arch.fp8_amax = tr.activation_amax(arch, w, boards)
+            ref = oracle.OracleNetwork(arch, w, threads=16).evaluate(boards, legal)
+            ref_q = oracle.OracleNetwork(arch, weights.fp8_weights(w), threads=16).evaluate(boards, legal)
+            cache[(d, heads, ff)] = (arch, w, boards, legal, counts, ref, ref_q)
+        return cache[(d, heads, ff)]
+
+    return get
+
+
+@pytest.mark.parametrize("d,heads,ff", [(64, 2, 256), (128, 2, 512), (256, 8, 1024), (320, 5, 1280),
+                                         (384, 6, 1536), (448, 7, 1792), (640, 10, 2560), (768, 12, 3072),
+                                         (1024, 16, 4096)])
+@pytest.mark.parametrize("precision", ["bf16", "fp8w", "fp8x2"])
+def test_every_supported_width(width_cases, d, heads, ff, precision):
+    """Every d_model the kernels are built for (head dims 32 and 64; `small` and `nano` are covered
+    above) meets the oracle bounds in each precision that meets them on the main cards."""
+    arch, w, boards, legal, counts, ref, ref_q = width_cases(d, heads, ff)
+    ref_p, ref_w = ref if precision == "bf16" else ref_q
+    net = B200Network(arch, w, max_batch=128, precision=precision)
+    priors, wdl = net.evaluate_packed(boards, legal)
+    net.close()
+    check_against(priors, wdl, ref_p, ref_w, counts, precision, arch, w, boards, legal)
+
+
 def test_biases_and_norm_parameters_are_applied():
     arch = model.nano()
     w = weights.random_init(arch, seed=5, bias_std=0.05, norm_std=0.2)

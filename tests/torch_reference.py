@@ -99,13 +99,24 @@ def quantise(x: torch.Tensor, mode: str | None, amax: float) -> torch.Tensor:
     return (e4m3_round(xb / s) * s).reshape(x.shape)
 
 
-def forward_quantised(arch, w, boards: np.ndarray, sites: dict, device="cpu", resid16: bool = True):
+def activation_amax(arch, w, boards: np.ndarray, device="cpu") -> list[list[float]]:
+    """Per layer the largest |value| at the four GEMM inputs (norm1 out, attention out, norm2 out,
+    GELU out) of the float32 forward on `boards`: a card's FP8 calibration
+    (`encoder.fp8.activation_amax`, src/net/model.rs:87-95) for a network built in a test."""
+    rows: list[list[float]] = []
+    forward_quantised(arch, w, boards, {}, device=device, record=rows)
+    return rows
+
+
+def forward_quantised(arch, w, boards: np.ndarray, sites: dict, device="cpu", resid16: bool = True,
+                      record: list | None = None):
     """Policy logits [n, 4672] and value logits [n, 3] in float32 with the four GEMM inputs of every
     layer quantised as `sites` says ({"n1": norm1 out, "at": attention out, "n2": norm2 out, "ge":
     GELU out} -> a `quantise` mode; missing sites stay float32) and, with `resid16`, the residual
     stream rounded to f16 after every update as the GPU keeps it. Weights are used as given (pass
     e4m3-quantised weights for the FP8 precisions). A simulation of the arithmetic of each
-    precision, for the precision study in tests/test_precision.py and the GPU tests."""
+    precision, for the precision study in tests/test_precision.py and the GPU tests. With
+    `record`, appends each layer's four site maxima (before quantisation) to it."""
     dev = torch.device(device)
     T = lambda name: torch.from_numpy(np.ascontiguousarray(w[name], dtype=np.float32)).to(dev)  # noqa: E731
     b = torch.from_numpy(boards.astype(np.int64)).to(dev)
@@ -126,15 +137,19 @@ def forward_quantised(arch, w, boards: np.ndarray, sites: dict, device="cpu", re
     for i in range(arch.n_layers):
         p = f"encoder.layers.{i}."
         am = amax[i] if amax is not None else [1.0] * 4
-        h = quantise(ln(x, p + "norm1"), sites.get("n1"), am[0])
+        seen = []
+        site = lambda v, key, j: (seen.append(float(v.abs().max())), quantise(v, sites.get(key), am[j]))[1]  # noqa: E731
+        h = site(ln(x, p + "norm1"), "n1", 0)
         qkv = h @ T(p + "self_attn.in_proj_weight").T + T(p + "self_attn.in_proj_bias")
         q, k, v = (qkv[..., j * d:(j + 1) * d].reshape(n, t, H, hd).transpose(1, 2) for j in range(3))
         a = torch.softmax(q @ k.transpose(-1, -2) / math.sqrt(hd), -1) @ v
-        a = quantise(a.transpose(1, 2).reshape(n, t, d), sites.get("at"), am[1])
+        a = site(a.transpose(1, 2).reshape(n, t, d), "at", 1)
         x = f16(x + a @ T(p + "self_attn.out_proj.weight").T + T(p + "self_attn.out_proj.bias"))
-        h = quantise(ln(x, p + "norm2"), sites.get("n2"), am[2])
-        f = quantise(gelu(h @ T(p + "linear1.weight").T + T(p + "linear1.bias")), sites.get("ge"), am[3])
+        h = site(ln(x, p + "norm2"), "n2", 2)
+        f = site(gelu(h @ T(p + "linear1.weight").T + T(p + "linear1.bias")), "ge", 3)
         x = f16(x + f @ T(p + "linear2.weight").T + T(p + "linear2.bias"))
+        if record is not None:
+            record.append(seen)
     h = ln(x, "final_norm")
     sq = ln(h[:, s0:s0 + 64], "policy_head.norm")
     policy = (sq @ T("policy_head.proj.weight").T + T("policy_head.proj.bias")).reshape(n, 64 * 73)
