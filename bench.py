@@ -630,7 +630,8 @@ def run_wholebox(args):
 def run_gemm(args):
     """Our tcgen05 GEMM (through mrn_test_gemm) beside cuBLAS on the encoder's four GEMM shapes at
     this batch: with `--precision fp8` e4m3 operands against cuBLASLt FP8 (torch._scaled_mm, e4m3 x
-    e4m3 -> bf16 with a bias), otherwise bf16 operands (kind::f16) against cuBLAS bf16
+    e4m3 -> bf16 with a bias; `fp8x2`: ours on two-term e4m3 A, two MMAs per K-step, cuBLASLt on one
+    term), otherwise bf16 operands (kind::f16) against cuBLAS bf16
     (torch.addmm). cuBLAS gets the plain bias epilogue on every shape (its residual would be a
     bf16 beta=1 add); ours runs the epilogue the forward pass uses (bias->bf16, GELU->e4m3 or bf16,
     f16 residual add). CUDA events, after warm-up; inputs > L2."""
@@ -646,31 +647,34 @@ def run_gemm(args):
     lib = _lib.load_test()
     stream = torch.cuda.current_stream().cuda_stream
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    fp8 = args.precision == "fp8"
+    fp8 = args.precision in ("fp8", "fp8x2")
+    x2 = args.precision == "fp8x2"  # two-term e4m3 A [M, 2K]; FFN1 writes two-term e4m3 [M, 2N]
     out = []
     for name, N, K, epi, odt in [("qkv", 3 * d, d, 0, torch.bfloat16), ("out_proj", d, d, 3, torch.float16),
-                                 ("ffn1", ff, d, 2 if fp8 else 1, torch.uint8 if fp8 else torch.bfloat16),
+                                 ("ffn1", ff, d, 7 if x2 else 2 if fp8 else 1, torch.uint8 if fp8 else torch.bfloat16),
                                  ("ffn2", d, ff, 3, torch.float16)]:
         if fp8:
-            a = (torch.randn(M, K, device=dev) * 0.5).to(torch.float8_e4m3fn)
+            a = (torch.randn(M, 2 * K if x2 else K, device=dev) * 0.5).to(torch.float8_e4m3fn)
             b = (torch.randn(N, K, device=dev) * 0.5).to(torch.float8_e4m3fn)
         else:
             a = (torch.randn(M, K, device=dev) * 0.5).to(torch.bfloat16)
             b = (torch.randn(N, K, device=dev) * 0.05).to(torch.bfloat16)
         bias = torch.randn(N, device=dev)
-        o = torch.zeros(M, N, device=dev, dtype=odt)
+        ldo = 2 * N if x2 and epi == 7 else N
+        o = torch.zeros(M, ldo, device=dev, dtype=odt)
 
         def ours():
-            rc = lib.mrn_test_gemm(int(fp8), epi, a.data_ptr(), b.data_ptr(), bias.data_ptr(), o.data_ptr(), N, M, N,
-                                   K, 1e-3 if fp8 else 1.0, 10.0, ctypes.c_void_p(status.data_ptr()),
-                                   ctypes.c_void_p(stream))
+            rc = lib.mrn_test_gemm(2 if x2 else int(fp8), epi, a.data_ptr(), b.data_ptr(), bias.data_ptr(),
+                                   o.data_ptr(), ldo, M, N, K, 1e-3 if fp8 else 1.0, 10.0,
+                                   ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(stream))
             assert rc == 0, lib.mrn_test_last_error().decode()
 
         one, bias16 = torch.tensor(1.0, device=dev), bias.to(torch.bfloat16)
+        a1 = a[:, :K].contiguous() if x2 else a  # cuBLASLt gets one e4m3 term
 
         def cublas():
             if fp8:
-                torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, bias=bias16, out_dtype=torch.bfloat16)
+                torch._scaled_mm(a1, b.t(), scale_a=one, scale_b=one, bias=bias16, out_dtype=torch.bfloat16)
             else:
                 torch.addmm(bias16, a, b.t())
 
@@ -690,7 +694,8 @@ def run_gemm(args):
         row["cublaslt_tflops"] = 2 * M * N * K / row["cublaslt_us"] / 1e6
         assert int(status.item()) == 0
         out.append(row)
-    print(json.dumps({"mode": "gemm", "net": args.net, "batch": args.batch, "dtype": "e4m3" if fp8 else "bf16",
+    print(json.dumps({"mode": "gemm", "net": args.net, "batch": args.batch,
+                      "dtype": "e4m3x2" if x2 else "e4m3" if fp8 else "bf16",
                       "shapes": out}), flush=True)
 
 
