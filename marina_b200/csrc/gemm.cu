@@ -73,14 +73,35 @@ cudaError_t prepare_pair() {
                               PairShapeOf<Epi, X2>::kSmemBytes);
 }
 
-// Smallest K planned on CTA pairs (N a multiple of 256): MRN_GEMM_PAIR=0 never, =2 from K = 512,
-// otherwise from K = 1024.
-int pair_min_k() {
-  static const int k = [] {
+// MRN_GEMM_PAIR: 0 never plan CTA pairs, 1 only from K = 1024, 2 from K = 512 for every epilogue;
+// unset (-1): the measured rule of use_pair.
+int pair_mode() {
+  static const int m = [] {
     const char* e = getenv("MRN_GEMM_PAIR");
-    return e && e[0] == '0' ? 1 << 30 : e && e[0] == '2' ? 512 : 1024;
+    return e && e[0] >= '0' && e[0] <= '2' ? e[0] - '0' : -1;
   }();
-  return k;
+  return m;
+}
+
+// Rows from which the bias epilogue (QKV) runs on CTA pairs at K = 512.
+constexpr int kPairBiasMinRows = 65536;
+
+// CTA pairs (256 x 256 tiles, each CTA loading half of B) need N a multiple of 256. They halve
+// the operand bytes per FLOP and deepen the ring, which pays for long main loops (K >= 1024:
+// FFN2), for the residual epilogue from K = 512 (out-proj: 10-20% faster at every batch from 256
+// to 4096 positions) and for the bias epilogue from K = 512 once M is large (QKV: level at 512
+// positions, 2-4% faster from 1024, 6% slower at 256); the GELU epilogues stay on single CTAs
+// (FFN1 1-10% slower on pairs).
+bool use_pair(const GemmArgs& a) {
+  if (a.n % 256 != 0) return false;
+  switch (pair_mode()) {
+    case 0: return false;
+    case 1: return a.k >= 1024;
+    case 2: return a.k >= 512;
+  }
+  if (a.k >= 1024) return true;
+  if (a.k < 512) return false;
+  return a.epi == Epilogue::kResidual || (a.epi == Epilogue::kBias && a.m >= kPairBiasMinRows);
 }
 
 template <int BN, bool FP8, bool X2>
@@ -169,9 +190,7 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
     snprintf(err, 256, "gemm: output/bias misaligned or ldo %d < N %d", args.ldo, args.n);
     return false;
   }
-  // CTA pairs halve the operand bytes per FLOP, which pays where the main loop is long (FFN2,
-  // K = 4d); with K = d the two CTAs' coupled epilogues cost more than that saves.
-  plan->pair = args.n % 256 == 0 && args.k >= pair_min_k();
+  plan->pair = use_pair(args);
   // The memory-bound residual GEMMs with a short K (out-proj) run 128-column tiles with four
   // TMEM accumulators: the reduce-add stores drain behind three tiles of MMAs.
   if (!plan->pair && args.epi == Epilogue::kResidual && args.k < 1024 && args.n % 128 == 0) plan->bn = 128;

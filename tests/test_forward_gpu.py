@@ -418,14 +418,15 @@ def _check_plans_against_oracle(outs, net, precision):
 
 @pytest.mark.parametrize("net,precision", [("small", "fp8w"), ("small", "bf16"), ("small", "fp8"), ("small", "fp8x2")])
 def test_cta_pair_plans(tmp_path, net, precision):
-    """The GEMMs planned on CTA pairs from K = 512 (MRN_GEMM_PAIR=2: QKV and FFN1 as well), only from
-    K = 1024 (the default below, FFN2) and never (MRN_GEMM_PAIR=0) agree with each other to f32
-    accumulation order and each meets the oracle bounds."""
+    """The GEMMs planned on CTA pairs by the default rule (FFN2, out-proj; QKV only from 65,536 rows),
+    from K = 512 for every epilogue (MRN_GEMM_PAIR=2: QKV and FFN1 as well), only from K = 1024
+    (MRN_GEMM_PAIR=1, FFN2) and never (MRN_GEMM_PAIR=0) agree with each other to f32 accumulation
+    order and each meets the oracle bounds."""
     outs = _run_plans(tmp_path, net, precision, {"never": {"MRN_GEMM_PAIR": "0"}, "k1024": {"MRN_GEMM_PAIR": "1"},
-                                                 "k512": {"MRN_GEMM_PAIR": "2"}})
+                                                 "k512": {"MRN_GEMM_PAIR": "2"}, "default": {}})
     layers = card(net).n_layers
     counts = outs["never"]["counts"]
-    for key in ("k1024", "k512"):
+    for key in ("k1024", "k512", "default"):
         assert int(outs[key]["launches"]) == 7 * layers + 3
         m = compare(outs[key]["priors"], outs[key]["wdl"], outs["never"]["priors"], outs["never"]["wdl"], counts)
         print(key, m)
