@@ -88,10 +88,11 @@ constexpr int kPairBiasMinRows = 65536;
 
 // CTA pairs (256 x 256 tiles, each CTA loading half of B) need N a multiple of 256. They halve
 // the operand bytes per FLOP and deepen the ring, which pays for long main loops (K >= 1024:
-// FFN2), for the residual epilogue from K = 512 (out-proj: 10-20% faster at every batch from 256
-// to 4096 positions) and for the bias epilogue from K = 512 once M is large (QKV: level at 512
-// positions, 2-4% faster from 1024, 6% slower at 256); the GELU epilogues stay on single CTAs
-// (FFN1 1-10% slower on pairs).
+// FFN2) and, with bf16 operands, for the residual epilogue from K = 512 (out-proj: 10-20% faster
+// at every batch from 256 to 4096 positions) and for the bias epilogue from K = 512 once M is
+// large (QKV: level at 512 positions, 2-4% faster from 1024, 6% slower at 256). The GELU
+// epilogues stay on single CTAs (FFN1 1-10% slower on pairs), and so do e4m3 operands at K = 512
+// (the fp8 pass 231k -> 224k evals/s with those two on pairs).
 bool use_pair(const GemmArgs& a) {
   if (a.n % 256 != 0) return false;
   switch (pair_mode()) {
@@ -100,7 +101,7 @@ bool use_pair(const GemmArgs& a) {
     case 2: return a.k >= 512;
   }
   if (a.k >= 1024) return true;
-  if (a.k < 512) return false;
+  if (a.k < 512 || a.fp8) return false;
   return a.epi == Epilogue::kResidual || (a.epi == Epilogue::kBias && a.m >= kPairBiasMinRows);
 }
 
