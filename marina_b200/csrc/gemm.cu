@@ -91,8 +91,9 @@ constexpr int kPairBiasMinRows = 65536;
 // FFN2) and, with bf16 operands, for the residual epilogue from K = 512 (out-proj: 10-20% faster
 // at every batch from 256 to 4096 positions) and for the bias epilogue from K = 512 once M is
 // large (QKV: level at 512 positions, 2-4% faster from 1024, 6% slower at 256). The GELU
-// epilogues stay on single CTAs (FFN1 1-10% slower on pairs), and so do e4m3 operands at K = 512
-// (the fp8 pass 231k -> 224k evals/s with those two on pairs).
+// epilogues stay on single CTAs (FFN1 1-10% slower on pairs), and so do one-term e4m3 operands
+// at K = 512 (batch 4096: QKV 246 -> 281 us, out-proj 114 -> 133 on pairs); two-term e4m3 runs
+// the out-proj on pairs (159 -> 150 us) and QKV on single CTAs (350 -> 362 on pairs).
 bool use_pair(const GemmArgs& a) {
   if (a.n % 256 != 0) return false;
   switch (pair_mode()) {
@@ -101,8 +102,9 @@ bool use_pair(const GemmArgs& a) {
     case 2: return a.k >= 512;
   }
   if (a.k >= 1024) return true;
-  if (a.k < 512 || a.fp8) return false;
-  return a.epi == Epilogue::kResidual || (a.epi == Epilogue::kBias && a.m >= kPairBiasMinRows);
+  if (a.k < 512) return false;
+  if (a.epi == Epilogue::kResidual) return !a.fp8 || a.x2;
+  return a.epi == Epilogue::kBias && !a.fp8 && a.m >= kPairBiasMinRows;
 }
 
 template <int BN, bool FP8, bool X2>

@@ -46,9 +46,9 @@ struct GemmPlan {
 };
 
 // Widest supported N tile (256, 192, 128, 64) dividing n; 0 if none. Plans for N a multiple of
-// 256 run on CTA pairs for K >= 1024, and (bf16 operands) from K = 512 for the residual epilogue
-// and for the bias epilogue with M >= 65,536 rows (MRN_GEMM_PAIR=0: never; =1: K >= 1024 only;
-// =2: from K = 512).
+// 256 run on CTA pairs for K >= 1024, and from K = 512 for the residual epilogue (bf16 or
+// two-term e4m3 operands) and for the bias epilogue with bf16 operands on M >= 65,536 rows
+// (MRN_GEMM_PAIR=0: never; =1: K >= 1024 only; =2: from K = 512).
 int gemm_pick_bn(int n);
 
 // Validate shapes and alignment and build the tensor maps. `err` (>= 256 bytes) receives a
