@@ -197,6 +197,18 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
   // The memory-bound residual GEMMs with a short K (out-proj) run 128-column tiles with four
   // TMEM accumulators: the reduce-add stores drain behind three tiles of MMAs.
   if (!plan->pair && args.epi == Epilogue::kResidual && args.k < 1024 && args.n % 128 == 0) plan->bn = 128;
+  // Small batches: the narrowest tile (64, then 128 columns) whose tiles still fit in one wave of
+  // the SMs. More SMs share the GEMM, and the narrower stages hold more of its K loop in flight
+  // (batch 1: 0.585 -> 0.513 ms per pass with 64-column tiles; batch 16: 0.638 -> 0.595 with 128;
+  // from batch 64 the widest tile is faster).
+  if (!plan->pair) {
+    const int m_tiles = (args.m + kTileM - 1) / kTileM;
+    for (int bn : {64, 128})
+      if (bn < plan->bn && args.n % bn == 0 && m_tiles * (args.n / bn) <= num_sms) {
+        plan->bn = bn;
+        break;
+      }
+  }
   // Two-term A: [M, 2K] with each row's K hi codes then its K lo codes, read through two maps.
   const uint64_t a_row = args.x2 ? 2 * static_cast<uint64_t>(args.k) : 0;
   if (!make_kmajor_map(&plan->map_a, args.a, eb, args.m, args.k, kTileM, a_row) ||
