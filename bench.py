@@ -664,7 +664,7 @@ def run_gemm(args):
         o = torch.zeros(M, ldo, device=dev, dtype=odt)
 
         def ours():
-            rc = lib.mrn_test_gemm(2 if x2 else int(fp8), epi, a.data_ptr(), b.data_ptr(), bias.data_ptr(),
+            rc = lib.mrn_test_gemm(2 if x2 else int(fp8), epi, -1, a.data_ptr(), b.data_ptr(), bias.data_ptr(),
                                    o.data_ptr(), ldo, M, N, K, 1e-3 if fp8 else 1.0, 10.0,
                                    ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(stream))
             assert rc == 0, lib.mrn_test_last_error().decode()

@@ -24,9 +24,11 @@ extern "C" {
  * types: 0 bf16, 1 e4m3, 2 e4m3 weights with a two-term e4m3 `a` [m, 2k] (each row's k hi codes,
  * then its k lo codes; the product is taken as (hi + lo) . b). `epilogue` is 0 bias->bf16,
  * 1 GELU->bf16, 2 GELU->e4m3 (x inv_q), 3 residual add into f16 `out`, 5 / 6 the tanh-form GELU
- * into bf16 / e4m3, 7 / 8 the erf / tanh GELU into two-term e4m3 (x inv_q) [m, 2n] (fp8 = 2). */
-MRN_TEST_API int mrn_test_gemm(int fp8, int epilogue, const void* a, const void* b, const float* bias, void* out,
-                               int ldo, int m, int n, int k, float scale, float inv_q, int* status, void* stream);
+ * into bf16 / e4m3, 7 / 8 the erf / tanh GELU into two-term e4m3 (x inv_q) [m, 2n] (fp8 = 2).
+ * `pair`: -1 the evaluator's planning rule, 0 single-CTA tiles, 1 CTA-pair tiles (N % 256 == 0). */
+MRN_TEST_API int mrn_test_gemm(int fp8, int epilogue, int pair, const void* a, const void* b, const float* bias,
+                               void* out, int ldo, int m, int n, int k, float scale, float inv_q, int* status,
+                               void* stream);
 
 /* A bf16 bias GEMM (k < 1024, the single-CTA kernel) whose TMA producer issues no loads, with
  * every bounded wait limited to `wait_limit_ns`: the MMA and epilogue warps' waits run out, the

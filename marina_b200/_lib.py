@@ -98,8 +98,8 @@ SIGNATURES = {
 }
 
 TEST_SIGNATURES = {
-    "mrn_test_gemm": (c_int, [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
-                              c_float, c_float, c_void_p, c_void_p]),
+    "mrn_test_gemm": (c_int, [c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                              c_int, c_float, c_float, c_void_p, c_void_p]),
     "mrn_test_gemm_wait_expiry": (c_int, [ctypes.c_ulonglong, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                           c_int, c_void_p, c_void_p]),
     "mrn_test_attention": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_void_p, c_void_p]),

@@ -52,9 +52,11 @@ extern "C" {
 
 MRN_TEST_API const char* mrn_test_last_error(void) { return g_test_error; }
 
-MRN_TEST_API int mrn_test_gemm(int fp8, int epilogue, const void* a, const void* b, const float* bias, void* out,
-                               int ldo, int m, int n, int k, float scale, float inv_q, int* status, void* stream) {
+MRN_TEST_API int mrn_test_gemm(int fp8, int epilogue, int pair, const void* a, const void* b, const float* bias,
+                               void* out, int ldo, int m, int n, int k, float scale, float inv_q, int* status,
+                               void* stream) {
   if (!prepare()) return fail("gemm_prepare_device failed");
+  if (pair < -1 || pair > 1) return fail("pair must be -1 (the planning rule), 0 (single CTAs) or 1 (CTA pairs)");
   mrn::GemmArgs args;
   args.a = a;
   args.b = b;
@@ -64,6 +66,7 @@ MRN_TEST_API int mrn_test_gemm(int fp8, int epilogue, const void* a, const void*
   if (fp8 < 0 || fp8 > 2) return fail("fp8 must be 0 (bf16), 1 (e4m3) or 2 (two-term e4m3 A)");
   args.fp8 = fp8 != 0;
   args.x2 = fp8 == 2;
+  args.pair = pair;
   args.epi = static_cast<mrn::Epilogue>(epilogue);
   args.out = out;
   args.ldo = ldo;

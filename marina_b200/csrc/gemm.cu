@@ -93,14 +93,19 @@ constexpr int kPairBiasMinRows = 65536;
 // large (QKV: level at 512 positions, 2-4% faster from 1024, 6% slower at 256). The GELU
 // epilogues stay on single CTAs (FFN1 1-10% slower on pairs), and so do one-term e4m3 operands
 // at K = 512 (batch 4096: QKV 246 -> 281 us, out-proj 114 -> 133 on pairs); two-term e4m3 runs
-// the out-proj on pairs (159 -> 150 us) and QKV on single CTAs (350 -> 362 on pairs).
-bool use_pair(const GemmArgs& a) {
-  if (a.n % 256 != 0) return false;
+// the out-proj on pairs (159 -> 150 us) and QKV on single CTAs (350 -> 362 on pairs). Pairs also
+// need a full wave of 128-row tiles (M >= 128 rows x SMs): with fewer, single CTAs on narrow tiles
+// spread the GEMM over more SMs (batch 1: 0.517 -> 0.445 ms per pass, 16: 0.596 -> 0.515, 64:
+// 0.763 -> 0.703; level at 256).
+bool use_pair(const GemmArgs& a, int num_sms) {
+  if (a.n % 256 != 0 || a.pair == 0) return false;
+  if (a.pair == 1) return true;
   switch (pair_mode()) {
     case 0: return false;
     case 1: return a.k >= 1024;
     case 2: return a.k >= 512;
   }
+  if (a.m < kTileM * num_sms) return false;
   if (a.k >= 1024) return true;
   if (a.k < 512) return false;
   if (a.epi == Epilogue::kResidual) return !a.fp8 || a.x2;
@@ -193,7 +198,7 @@ bool gemm_plan(GemmPlan* plan, const GemmArgs& args, int num_sms, char* err) {
     snprintf(err, 256, "gemm: output/bias misaligned or ldo %d < N %d", args.ldo, args.n);
     return false;
   }
-  plan->pair = use_pair(args);
+  plan->pair = use_pair(args, num_sms);
   // The memory-bound residual GEMMs with a short K (out-proj) run 128-column tiles with four
   // TMEM accumulators: the reduce-add stores drain behind three tiles of MMAs.
   if (!plan->pair && args.epi == Epilogue::kResidual && args.k < 1024 && args.n % 128 == 0) plan->bn = 128;

@@ -25,6 +25,7 @@ struct GemmArgs {
   int m = 0, n = 0, k = 0;
   bool fp8 = false;          // operands are e4m3 (kind::f8f6f4) instead of bf16 (kind::f16)
   bool x2 = false;           // (fp8) A is two-term e4m3 [M, 2K]: each row's K hi codes, then its K lo codes
+  int pair = -1;             // CTA pairs: -1 the planning rule, 0 never, 1 whenever N % 256 == 0
   Epilogue epi = Epilogue::kBias;
   void* out = nullptr;       // bf16 / e4m3 output, or the f16 residual stream
   int ldo = 0;               // row stride of `out` in elements
@@ -46,9 +47,10 @@ struct GemmPlan {
 };
 
 // Widest supported N tile (256, 192, 128, 64) dividing n; 0 if none. Plans for N a multiple of
-// 256 run on CTA pairs for K >= 1024, and from K = 512 for the residual epilogue (bf16 or
-// two-term e4m3 operands) and for the bias epilogue with bf16 operands on M >= 65,536 rows
-// (MRN_GEMM_PAIR=0: never; =1: K >= 1024 only; =2: from K = 512).
+// 256 and M >= 128 rows x SMs run on CTA pairs for K >= 1024, and from K = 512 for the residual
+// epilogue (bf16 or two-term e4m3 operands) and for the bias epilogue with bf16 operands on
+// M >= 65,536 rows (MRN_GEMM_PAIR=0: never; =1: K >= 1024 at any M; =2: from K = 512 at any M).
+// Without pairs, small batches take the narrowest tile whose tiles fit in one wave.
 int gemm_pick_bn(int n);
 
 // Validate shapes and alignment and build the tensor maps. `err` (>= 256 bytes) receives a

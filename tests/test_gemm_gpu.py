@@ -16,7 +16,8 @@ EPI_BIAS, EPI_GELU_BF16, EPI_GELU_E4M3, EPI_RESIDUAL = 0, 1, 2, 3
 EPI_GELU_TANH_BF16, EPI_GELU_TANH_E4M3 = 5, 6
 EPI_GELU_E4M3X2, EPI_GELU_TANH_E4M3X2 = 7, 8
 
-# (M, N, K): QKV, out-proj, FFN1, FFN2 of both nets; M = positions x 65.
+# (M, N, K): QKV, out-proj, FFN1, FFN2 of both nets; M = positions x 65. Shapes with N % 256 == 0
+# run on single CTAs and on CTA pairs (`pair` 0 and 1), whatever the planning rule would pick.
 SHAPES = [
     (65 * 3, 576, 192), (65 * 3, 192, 192), (65 * 3, 768, 192), (65 * 3, 192, 768),
     (65 * 7, 1536, 512), (65 * 7, 512, 512), (65 * 7, 2048, 512), (65 * 7, 512, 2048),
@@ -26,15 +27,21 @@ SHAPES = [
 ]
 
 
-def _run(fp8, epi, a, b, bias, out, ldo, m, n, k, scale=1.0, inv_q=1.0):
+def _run(fp8, epi, a, b, bias, out, ldo, m, n, k, scale=1.0, inv_q=1.0, pair=-1):
+    """One GEMM through the test library; `pair` -1 the planning rule, 0 single CTAs, 1 CTA pairs."""
     lib = _lib.load_test()
     status = torch.zeros(1, dtype=torch.int32, device=a.device)
     stream = torch.cuda.current_stream().cuda_stream
-    rc = lib.mrn_test_gemm(int(fp8), epi, a.data_ptr(), b.data_ptr(), bias.data_ptr(), out.data_ptr(), ldo, m, n, k,
-                           scale, inv_q, ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(stream))
+    rc = lib.mrn_test_gemm(int(fp8), epi, pair, a.data_ptr(), b.data_ptr(), bias.data_ptr(), out.data_ptr(), ldo, m,
+                           n, k, scale, inv_q, ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(stream))
     assert rc == 0, lib.mrn_test_last_error().decode()
     torch.cuda.synchronize()
     assert int(status.item()) == 0, f"device status {int(status.item())}"
+
+
+def _pairs(shapes):
+    """(m, n, k, pair) for each shape: single CTAs, and CTA pairs where N % 256 == 0."""
+    return [(m, n, k, p) for m, n, k in shapes for p in ((0, 1) if n % 256 == 0 else (0,))]
 
 
 def _within(got, ref, tol, what=""):
@@ -82,14 +89,14 @@ def _x2_operands(m, n, k, seed):
     return a2, b8.view(torch.uint8), hi.float() + lo.float(), b8.float(), hi.float(), bias
 
 
-@pytest.mark.parametrize("m,n,k", SHAPES)
-def test_two_term_operands(cuda, m, n, k):
+@pytest.mark.parametrize("m,n,k,pair", _pairs(SHAPES))
+def test_two_term_operands(cuda, m, n, k, pair):
     """Two-term e4m3 A: the product is (hi + lo) . b, held to the bf16 output's rounding, which is
     far below what dropping the lo term would cost (about 2^-5 of each product)."""
     a2, b, af, bf, hif, bias = _x2_operands(m, n, k, seed=m + 2 * n + k)
     scale = 2.0 ** -12
     out = torch.full((m, n), float("nan"), device=cuda, dtype=torch.bfloat16)
-    _run(2, EPI_BIAS, a2, b, bias, out, n, m, n, k, scale=scale)
+    _run(2, EPI_BIAS, a2, b, bias, out, n, m, n, k, scale=scale, pair=pair)
     ref = (af @ bf.T) * scale + bias
     tol = ref.abs() * 2 ** -8 + 1e-4 * float(ref.abs().max())
     _within(out.float(), ref, tol, "two-term bias")
@@ -98,21 +105,21 @@ def test_two_term_operands(cuda, m, n, k):
     assert not bool(((hi_only - ref).abs() <= tol).all())
     x0 = torch.randn(m, n, device=cuda).half()
     x = x0.clone()
-    _run(2, EPI_RESIDUAL, a2, b, bias, x, n, m, n, k, scale=scale)
+    _run(2, EPI_RESIDUAL, a2, b, bias, x, n, m, n, k, scale=scale, pair=pair)
     delta = (af @ bf.T) * scale + bias
     ref = x0.float() + delta
     _within(x.float(), ref, (ref.abs() + delta.abs()) * 2 ** -10 + 2 ** -14, "two-term residual")
 
 
-@pytest.mark.parametrize("m,n,k", [s for s in SHAPES if s[1] in (768, 2048, 256)])
+@pytest.mark.parametrize("m,n,k,pair", _pairs([s for s in SHAPES if s[1] in (768, 2048, 256)]))
 @pytest.mark.parametrize("epi", [EPI_GELU_E4M3X2, EPI_GELU_TANH_E4M3X2], ids=["erf", "tanh"])
-def test_gelu_two_term_epilogue(cuda, m, n, k, epi):
+def test_gelu_two_term_epilogue(cuda, m, n, k, pair, epi):
     """GELU into two-term e4m3 [m, 2n] (hi codes in columns [0, n), lo codes in [n, 2n)), from
     two-term operands, as FFN1 of the fp8x2 precision writes FFN2's input."""
     a2, b, af, bf, _, bias = _x2_operands(m, n, k, seed=19 + epi)
     scale, q = 2.0 ** -12, 0.01  # output value = (hi + lo) * q
     out = torch.full((m, 2 * n + 32), 0x55, device=cuda, dtype=torch.uint8)
-    _run(2, epi, a2, b, bias, out, 2 * n + 32, m, n, k, scale=scale, inv_q=1.0 / q)
+    _run(2, epi, a2, b, bias, out, 2 * n + 32, m, n, k, scale=scale, inv_q=1.0 / q, pair=pair)
     approx = "tanh" if epi == EPI_GELU_TANH_E4M3X2 else "none"
     ref = torch.nn.functional.gelu((af @ bf.T) * scale + bias, approximate=approx)
     assert float(ref.abs().max()) < 448 * q
@@ -124,33 +131,33 @@ def test_gelu_two_term_epilogue(cuda, m, n, k, epi):
 
 
 @pytest.mark.parametrize("fp8", [False, True], ids=["bf16", "e4m3"])
-@pytest.mark.parametrize("m,n,k", SHAPES)
-def test_bias_epilogue(cuda, fp8, m, n, k):
+@pytest.mark.parametrize("m,n,k,pair", _pairs(SHAPES))
+def test_bias_epilogue(cuda, fp8, m, n, k, pair):
     a, b, af, bf, bias = _operands(m, n, k, fp8, seed=m + n + k)
     scale = 0.125 if fp8 else 1.0
     out = torch.full((m, n), float("nan"), device=cuda, dtype=torch.bfloat16)
-    _run(fp8, EPI_BIAS, a, b, bias, out, n, m, n, k, scale=scale)
+    _run(fp8, EPI_BIAS, a, b, bias, out, n, m, n, k, scale=scale, pair=pair)
     ref = (af @ bf.T) * scale + bias
     err = (out.float() - ref).abs().max().item()
     assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
 
 
-@pytest.mark.parametrize("m,n,k", [s for s in SHAPES if s[1] in (768, 2048, 256)])
-def test_gelu_bf16_epilogue(cuda, m, n, k):
+@pytest.mark.parametrize("m,n,k,pair", _pairs([s for s in SHAPES if s[1] in (768, 2048, 256)]))
+def test_gelu_bf16_epilogue(cuda, m, n, k, pair):
     a, b, af, bf, bias = _operands(m, n, k, False, seed=7)
     out = torch.zeros((m, n), device=cuda, dtype=torch.bfloat16)
-    _run(False, EPI_GELU_BF16, a, b, bias, out, n, m, n, k)
+    _run(False, EPI_GELU_BF16, a, b, bias, out, n, m, n, k, pair=pair)
     ref = torch.nn.functional.gelu(af @ bf.T + bias)
     err = (out.float() - ref).abs().max().item()
     assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
 
 
-@pytest.mark.parametrize("m,n,k", [s for s in SHAPES if s[1] in (768, 2048, 256)])
-def test_gelu_e4m3_epilogue(cuda, m, n, k):
+@pytest.mark.parametrize("m,n,k,pair", _pairs([s for s in SHAPES if s[1] in (768, 2048, 256)]))
+def test_gelu_e4m3_epilogue(cuda, m, n, k, pair):
     a, b, af, bf, bias = _operands(m, n, k, True, seed=11)
     scale, q = 0.125, 0.05  # output value = code * q
     out = torch.zeros((m, n), device=cuda, dtype=torch.uint8)
-    _run(True, EPI_GELU_E4M3, a, b, bias, out, n, m, n, k, scale=scale, inv_q=1.0 / q)
+    _run(True, EPI_GELU_E4M3, a, b, bias, out, n, m, n, k, scale=scale, inv_q=1.0 / q, pair=pair)
     ref = torch.nn.functional.gelu((af @ bf.T) * scale + bias)
     got = out.view(torch.float8_e4m3fn).float() * q
     # one e4m3 rounding step (3 mantissa bits) plus saturation at 448 * q
@@ -178,13 +185,13 @@ def test_gelu_tanh_epilogues(cuda, m, n, k):
 
 
 @pytest.mark.parametrize("fp8", [False, True], ids=["bf16", "e4m3"])
-@pytest.mark.parametrize("m,n,k", [s for s in SHAPES if s[1] in (192, 512, 128)])
-def test_residual_epilogue(cuda, fp8, m, n, k):
+@pytest.mark.parametrize("m,n,k,pair", _pairs([s for s in SHAPES if s[1] in (192, 512, 128)]))
+def test_residual_epilogue(cuda, fp8, m, n, k, pair):
     a, b, af, bf, bias = _operands(m, n, k, fp8, seed=3)
     scale = 0.125 if fp8 else 1.0
     x0 = torch.randn(m, n, device=cuda).half()  # the residual stream is f16
     x = x0.clone()
-    _run(fp8, EPI_RESIDUAL, a, b, bias, x, n, m, n, k, scale=scale)
+    _run(fp8, EPI_RESIDUAL, a, b, bias, x, n, m, n, k, scale=scale, pair=pair)
     delta = (af @ bf.T) * scale + bias
     ref = x0.float() + delta
     # the f16 sum of x and the f16-rounded update: at most an f16 half-ulp of each, plus the

@@ -118,8 +118,8 @@ def test_bounded_wait_expiry_reports_a_device_fault_and_the_context_recovers(cud
 
     def plain():
         status.zero_()
-        rc = test.mrn_test_gemm(0, 0, a.data_ptr(), b.data_ptr(), bias.data_ptr(), out.data_ptr(), n, m, n, k, 1.0,
-                                1.0, ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(stream))
+        rc = test.mrn_test_gemm(0, 0, -1, a.data_ptr(), b.data_ptr(), bias.data_ptr(), out.data_ptr(), n, m, n, k,
+                                1.0, 1.0, ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(stream))
         torch.cuda.synchronize()
         assert rc == 0 and int(status.item()) == 0
         ref = a.float() @ b.float().T
