@@ -41,13 +41,15 @@ using mrn::Profiler;
 
 namespace {
 
+// Batch sizes a context captures a pass for: powers of two up to 256, then multiples of 128 (a
+// search's calls of a few thousand leaves pad by at most 128 positions).
 int bucket_for(int n) {
   if (n <= 256) {
     int b = 1;
     while (b < n) b <<= 1;
     return b;
   }
-  return (n + 255) / 256 * 256;
+  return (n + 127) / 128 * 128;
 }
 
 #define CK(call)                                                                                     \

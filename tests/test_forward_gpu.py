@@ -306,10 +306,10 @@ def test_buckets_and_padding():
     """Batch sizes that pad to a bucket give the oracle's answers for the real positions."""
     arch = model.nano()
     w = weights.random_init(arch, seed=0)
-    boards, legal, counts, _ = chess.random_positions(9, 300)
+    boards, legal, counts, _ = chess.random_positions(9, 512)
     net = B200Network(arch, w, max_batch=512, precision="bf16")
     ref_p, ref_w = oracle.OracleNetwork(arch, w, threads=16).evaluate(boards, legal)
-    for n in (3, 100, 257, 300):
+    for n in (3, 100, 257, 300, 385, 512):  # buckets 4, 128, 384, 384, 512, 512
         p, wd = net.evaluate_packed(boards[:n], legal[:n])
         check(compare(p, wd, ref_p[:n], ref_w[:n], counts[:n]), "bf16")
 
