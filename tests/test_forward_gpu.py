@@ -247,12 +247,29 @@ def test_biases_and_norm_parameters_are_applied():
     check(compare(priors, wdl, ref_p, ref_w, counts), "bf16")
 
 
-def test_raw_logits_match_the_oracle(nano_setup):
+@pytest.mark.parametrize("precision", ["bf16", "fp8w", "fp8x2"])
+def test_raw_logits_match_the_oracle(nano_setup, precision):
+    """`mrn_logits` (all 4,672 policy logits and the WDL logits) against the oracle's on the weights
+    the precision computes with (e4m3-quantised for fp8w / fp8x2), nano, 16 positions."""
     arch, w, boards, legal, counts = nano_setup
-    ref_policy, ref_value = oracle.OracleNetwork(arch, w, threads=8).logits(boards[:16])
-    policy, value = B200Network(arch, w, max_batch=64, precision="bf16").logits(boards[:16])
+    wr = w if precision == "bf16" else weights.fp8_weights(w)
+    ref_policy, ref_value = oracle.OracleNetwork(arch, wr, threads=8).logits(boards[:16])
+    policy, value = B200Network(arch, w, max_batch=64, precision=precision).logits(boards[:16])
+    print(precision, float(np.abs(policy - ref_policy).max()), float(np.abs(value - ref_value).max()))
     assert np.abs(policy - ref_policy).max() < 2e-2
     assert np.abs(value - ref_value).max() < 2e-2
+
+
+@pytest.mark.parametrize("precision", ["fp8w", "fp8x2"])
+def test_raw_logits_small(small_setup, precision):
+    """The same on the small net (12 layers), 32 positions: every policy logit, not only the legal
+    ones, within 5e-2 of the oracle's on the e4m3-quantised weights."""
+    arch, w, boards, legal, counts, ref, ref_q = small_setup
+    ref_policy, ref_value = oracle.OracleNetwork(arch, weights.fp8_weights(w), threads=16).logits(boards[:32])
+    policy, value = B200Network(arch, w, max_batch=32, precision=precision).logits(boards[:32])
+    print(precision, float(np.abs(policy - ref_policy).max()), float(np.abs(value - ref_value).max()))
+    assert np.abs(policy - ref_policy).max() < 5e-2
+    assert np.abs(value - ref_value).max() < 5e-2
 
 
 def test_edge_cases(nano_setup):
